@@ -1,0 +1,133 @@
+"""Top-k on B200: run({"x"}) -> {"values", "indices"}, K = 50.
+
+The reference's topk/candidate.py:66-81: the K largest entries of each row of 2-D x (fp32 or bf16), in descending
+order with ties broken by the lower index, values in x's dtype (bit-exact) and int64 indices, through the reference's
+C ABI (plan + launch, topk/kernel.cu:520,549). plan() is cached per (device, shape, dtype); rows split into several
+chunks merge through an int64 workspace and per-row int32 counters (zeroed once, left zeroed by the kernel), as the
+reference does. Launches of one shape on one stream are serialised, so the cached workspace is reused.
+params.json beside this module may set "log2_threads" (7..9), "log2_depth" (1..3) and "min_chunk" as the reference's
+does; the first two are validated by the C ABI only, min_chunk bounds the plan's chunk from below.
+
+Also here: topk(x, k) for any k <= 512, and the two halves of the vocab-sharded variant, shard_lists (local top-k of a
+column shard as sorted 64-bit composites with global column indices) and merge_lists (the final merge after those
+lists were gathered from every shard).
+"""
+
+import json
+import os
+
+import torch
+
+from . import _native
+
+K = 50
+MAX_K = 512
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_PARAMS_PATH = os.path.join(_HERE, "params.json")
+_params = {}
+if os.path.exists(_PARAMS_PATH):
+    with open(_PARAMS_PATH) as _handle:
+        _params = json.load(_handle)
+_THREADS = 1 << int(_params.get("log2_threads", 8))
+_DEPTH = 1 << int(_params.get("log2_depth", 2))
+_MIN_CHUNK = int(_params.get("min_chunk", 2048))
+_DTYPES = {torch.float32: 0, torch.bfloat16: 1}
+
+_counters = {}
+_plans = {}  # (device, rows, cols, dtype, k) -> (chunk, workspace)
+
+
+def _row_counters(device, rows):
+    counters = _counters.get(device)
+    if counters is None or counters.numel() < rows:
+        counters = torch.zeros(rows if rows > 4096 else 4096, dtype=torch.int32, device=device)
+        _counters[device] = counters
+    return counters
+
+
+def _plan(x, rows, cols, dtype, k):
+    key = (x.device, rows, cols, dtype, k)
+    hit = _plans.get(key)
+    if hit is not None:
+        return hit
+    lib = _native.load("topk")
+    with torch.cuda.device(x.device):
+        chunk = lib.plan(rows, cols, dtype, _THREADS, _DEPTH, _MIN_CHUNK)
+    nchunks = -(-cols // chunk)
+    work = torch.empty(rows * nchunks * k if nchunks > 1 else 1, dtype=torch.int64, device=x.device)
+    if len(_plans) > 16:
+        _plans.clear()
+    _plans[key] = (chunk, work)
+    return chunk, work
+
+
+def _check_x(x, k):
+    dtype = _DTYPES.get(x.dtype)
+    if dtype is None or x.dim() != 2 or x.shape[1] < k:
+        raise ValueError(f"topk candidate takes a 2-D fp32 or bf16 tensor with at least {k} columns, "
+                         f"got {x.dtype} with shape {tuple(x.shape)}")
+    if not 1 <= k <= MAX_K:
+        raise ValueError(f"topk candidate: k must be in [1, {MAX_K}], got {k}")
+    _native.require_cuda("topk", x)
+    return dtype
+
+
+def topk(x, k=K):
+    """The k largest entries of each row of x, descending, ties by lower index: (values, int64 indices)."""
+    dtype = _check_x(x, k)
+    x = x.contiguous()
+    rows, cols = x.shape
+    chunk, work = _plan(x, rows, cols, dtype, k)
+    counters = _row_counters(x.device, rows)
+    values = torch.empty((rows, k), dtype=x.dtype, device=x.device)
+    indices = torch.empty((rows, k), dtype=torch.int64, device=x.device)
+    lib = _native.load("topk")
+    with torch.cuda.device(x.device):
+        err = lib.launch(x.data_ptr(), values.data_ptr(), indices.data_ptr(), work.data_ptr(), counters.data_ptr(),
+                         rows, cols, k, dtype, _THREADS, _DEPTH, chunk, _native.stream_of(x))
+    _native.check(err)
+    return values, indices
+
+
+def run(inputs):
+    values, indices = topk(inputs["x"], K)
+    return {"values": values, "indices": indices}
+
+
+def shard_lists(x, col_offset, k=K, out=None):
+    """Local top-k of a column shard x [rows, cols] holding global columns [col_offset, col_offset + cols): returns
+    [rows, k] int64 tensor whose bits are the sorted 64-bit composites (key << 32 | ~global_index), zero padded."""
+    dtype = _check_x(x, k)
+    x = x.contiguous()
+    rows, cols = x.shape
+    chunk, work = _plan(x, rows, cols, dtype, k)
+    counters = _row_counters(x.device, rows)
+    lists = torch.empty((rows, k), dtype=torch.int64, device=x.device) if out is None else out
+    if lists.shape != (rows, k) or lists.dtype != torch.int64 or not lists.is_contiguous():
+        raise ValueError("topk shard: out must be a contiguous int64 [rows, k] tensor")
+    lib = _native.load("topk")
+    with torch.cuda.device(x.device):
+        err = lib.ckb_topk_shard_launch(x.data_ptr(), lists.data_ptr(), work.data_ptr(), counters.data_ptr(),
+                                        rows, cols, int(col_offset), k, dtype, chunk, _native.stream_of(x))
+    _native.check(err)
+    return lists
+
+
+def merge_lists(lists, dtype, k=K):
+    """Final top-k from gathered shard lists [nlists, rows, k] (int64 composites): (values in dtype, indices)."""
+    if dtype not in _DTYPES:
+        raise ValueError(f"topk merge: dtype {dtype}")
+    if lists.dtype != torch.int64 or lists.dim() != 3 or lists.shape[2] != k:
+        raise ValueError(f"topk merge: lists must be int64 [nlists, rows, {k}], got {lists.dtype} "
+                         f"{tuple(lists.shape)}")
+    _native.require_cuda("topk merge", lists)
+    lists = lists.contiguous()
+    nlists, rows, _ = lists.shape
+    values = torch.empty((rows, k), dtype=dtype, device=lists.device)
+    indices = torch.empty((rows, k), dtype=torch.int64, device=lists.device)
+    lib = _native.load("topk")
+    with torch.cuda.device(lists.device):
+        err = lib.ckb_topk_merge_launch(lists.data_ptr(), nlists, values.data_ptr(), indices.data_ptr(), rows, k,
+                                        _DTYPES[dtype], _native.stream_of(lists))
+    _native.check(err)
+    return values, indices

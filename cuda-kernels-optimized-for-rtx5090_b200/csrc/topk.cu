@@ -1,0 +1,551 @@
+// Row-wise top-k (largest k, sorted descending, ties broken by the lower index) of x[rows, cols], fp32 (dtype 0) or
+// bf16 (dtype 1), values bit-exact in x's dtype and int64 indices -- the reference's output contract
+// (topk/kernel.cu:1-3,436-441, topk/candidate.py:66-81).
+//
+// Order. Every element becomes a distinct 64-bit composite (order-preserving key of its float bits << 32 | ~index),
+// the same total order as the reference's pack() (topk/kernel.cu:56-60): larger value first, equal values by lower
+// index, NaN above +inf, -NaN below -inf. The top k of a row are its k largest composites.
+//
+// Algorithm (one CTA per chunk of a row, 512 threads):
+//   1. the chunk is pulled into shared memory by bulk copies (cp.async.bulk, several pieces on their own mbarriers);
+//   2. radix select on the composites: a 4096-bin histogram of the top 12 bits (built as the pieces land), the bin
+//      holding the k-th largest is found by a block suffix scan; if the elements at or above that bin exceed the
+//      candidate buffer (2048), the next digit of the composites inside that bin is histogrammed, and so on
+//      (digits 12/10/10 over the key, 12/10/10 over the index, so ties on the value resolve by index);
+//   3. one pass collects the composites at or above the selected bin's lower edge (typically k + a few dozen);
+//   4. a warp bitonic sort (up to 128 candidates, 4 per lane) or a block rank count leaves the chunk's top k sorted;
+//   5. a row split over several chunks writes each chunk's sorted top k to the workspace; the row's last CTA to finish
+//      (per-row counter, reset by that CTA) merges the sorted lists by rank (binary search of every candidate in the
+//      other lists) and decodes values and indices from the composites (x is not read again).
+// The vocab-sharded variant runs steps 1-5 on a column shard with a global column offset and stops at the sorted
+// composites; after an all-gather across GPUs the merge kernel ranks the per-GPU lists the same way.
+#include "ckb200_topk.h"
+#include "common.cuh"
+
+#include <climits>
+
+namespace ckb {
+
+__device__ unsigned int g_topk_status = 0u;
+
+namespace {
+
+typedef unsigned long long u64;
+
+constexpr int kThreads = 512;
+constexpr int kWarps = kThreads / 32;
+constexpr int kBins = 4096;            // largest digit: 12 bits
+constexpr int kCap = 2048;             // candidate buffer (aliases the histogram)
+constexpr int kMaxK = 512;
+constexpr int kPieces = 4;
+constexpr int kLevels = 6;
+constexpr int kChunkBytes = 48 * 1024;  // staged bytes per CTA: chunk + histogram keep 3 CTAs per SM
+constexpr int kMaxDataBytes = 160 * 1024;
+constexpr int kSortMax = 128;          // warp bitonic sort: 4 composites per lane
+
+__device__ __forceinline__ int level_shift(int L) {
+  return L == 0 ? 52 : L == 1 ? 42 : L == 2 ? 32 : L == 3 ? 20 : L == 4 ? 10 : 0;
+}
+__device__ __forceinline__ int level_width(int L) { return (L == 0 || L == 3) ? 12 : 10; }
+
+__device__ __forceinline__ unsigned order_key(unsigned bits) {
+  return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+}
+__device__ __forceinline__ unsigned key_bits(unsigned key) {  // inverse of order_key
+  return (key & 0x80000000u) ? (key & 0x7fffffffu) : ~key;
+}
+__device__ __forceinline__ u64 composite(unsigned key, unsigned idx) { return ((u64)key << 32) | (u64)(~idx); }
+
+// Keys of the elements in one 16-byte vector of staged data.
+__device__ __forceinline__ void keys16(const uint4& r, unsigned (&k)[4], const float*) {
+  k[0] = order_key(r.x); k[1] = order_key(r.y); k[2] = order_key(r.z); k[3] = order_key(r.w);
+}
+__device__ __forceinline__ void keys16(const uint4& r, unsigned (&k)[8], const __nv_bfloat16*) {
+  const unsigned w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    k[2 * j] = order_key(w[j] << 16);
+    k[2 * j + 1] = order_key(w[j] & 0xffff0000u);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ T decode_value(u64 c);
+template <>
+__device__ __forceinline__ float decode_value<float>(u64 c) { return __uint_as_float(key_bits((unsigned)(c >> 32))); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 decode_value<__nv_bfloat16>(u64 c) {
+  return __ushort_as_bfloat16((unsigned short)(key_bits((unsigned)(c >> 32)) >> 16));
+}
+__device__ __forceinline__ long long decode_index(u64 c) { return (long long)(~(unsigned)c); }
+
+// Number of entries greater than c in a descending list of n composites.
+__device__ __forceinline__ int count_greater(const u64* list, int n, u64 c) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (list[mid] > c) lo = mid + 1;
+    else hi = mid;
+  }
+  return lo;
+}
+
+// Sum of v over the threads with a higher threadIdx.x (all threads call it; two barriers).
+__device__ __forceinline__ unsigned block_suffix_excl(unsigned v, unsigned* warp_tot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  unsigned x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_down_sync(0xffffffffu, x, o);
+    if (lane + o < 32) x += y;
+  }
+  if (lane == 0) warp_tot[warp] = x;
+  __syncthreads();
+  unsigned higher = 0;
+  for (int w = warp + 1; w < kWarps; ++w) higher += warp_tot[w];
+  __syncthreads();
+  return higher + x - v;
+}
+
+// Descending bitonic sort of the 32 * P composites held P per lane (element lane * P + p), within one warp.
+template <int P>
+__device__ __forceinline__ void warp_sort_desc(u64 (&v)[P]) {
+  constexpr int N = 32 * P;
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1) {
+#pragma unroll
+    for (int j = size >> 1; j > 0; j >>= 1) {
+      if (j >= P) {
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+          const int e = lane * P + p;
+          const u64 o = __shfl_xor_sync(0xffffffffu, v[p], j / P);
+          const bool keep_max = ((e & j) == 0) == ((e & size) == 0);
+          v[p] = keep_max ? (v[p] > o ? v[p] : o) : (v[p] < o ? v[p] : o);
+        }
+      } else {
+#pragma unroll
+        for (int p = 0; p < P; ++p) {
+          if ((p & j) == 0) {
+            const int q = p | j;
+            const int e = lane * P + p;
+            const bool desc = (e & size) == 0;
+            const u64 a = v[p], b = v[q];
+            const bool swap = desc ? a < b : a > b;
+            v[p] = swap ? b : a;
+            v[q] = swap ? a : b;
+          }
+        }
+      }
+    }
+  }
+}
+
+struct ChunkArgs {
+  const void* x;
+  void* values;          // mode 0: [rows, k] in x's dtype
+  long long* indices;    // mode 0: [rows, k]
+  u64* lists;            // mode 1: [rows, k] sorted composites, zero padded
+  u64* work;             // [rows, nchunks, k] when a row has several chunks
+  unsigned* counters;    // [rows], zero on entry, left zero
+  long long col_offset;  // added to every column index
+  int cols, chunk, k, data_bytes, mode;
+};
+
+// Writes the row's final top k (sorted composites top[0, k)) in the requested form.
+template <typename T>
+__device__ __forceinline__ void emit(const ChunkArgs& a, long long row, int j, u64 c) {
+  if (a.mode == 0) {
+    reinterpret_cast<T*>(a.values)[row * a.k + j] = decode_value<T>(c);
+    a.indices[row * a.k + j] = decode_index(c);
+  } else {
+    a.lists[row * a.k + j] = c;
+  }
+}
+
+// Grid (nchunks, rows). kBulk: the chunk's rows are 16-byte aligned and sized, so bulk copies stage it; otherwise the
+// threads copy it element by element.
+template <typename T, bool kBulk>
+__global__ void __launch_bounds__(kThreads) topk_chunk(const ChunkArgs a) {
+  constexpr int V = VecN<T>::N;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t bars[kPieces];
+  __shared__ unsigned warp_tot[kWarps];
+  __shared__ int s_bin;
+  __shared__ unsigned s_above;
+  __shared__ int s_cnt;
+  __shared__ int s_last;
+
+  const T* tag = nullptr;
+  uint4* data = reinterpret_cast<uint4*>(smem_raw);
+  unsigned* hist = reinterpret_cast<unsigned*>(smem_raw + a.data_bytes);
+  u64* cand = reinterpret_cast<u64*>(hist);  // used only after the last histogram has been read
+  u64* top = reinterpret_cast<u64*>(smem_raw);  // used only after the last pass over the staged chunk
+
+  const long long row = blockIdx.y;
+  const int nchunks = gridDim.x;
+  const long long begin = (long long)blockIdx.x * a.chunk;
+  const int n = (int)min((long long)a.chunk, (long long)a.cols - begin);
+  const T* src = reinterpret_cast<const T*>(a.x) + row * a.cols + begin;
+  const int nv = (n + V - 1) / V;  // staged 16-byte vectors
+  const int pv = (nv + kPieces - 1) / kPieces;
+  const unsigned base_idx = (unsigned)(a.col_offset + begin);
+
+  // 1. Stage the chunk; zero the histogram meanwhile.
+  if constexpr (kBulk) {
+    if (threadIdx.x == 0) {
+#pragma unroll
+      for (int p = 0; p < kPieces; ++p) mbar_init(&bars[p], 1);
+      mbar_fence_init();
+#pragma unroll
+      for (int p = 0; p < kPieces; ++p) {
+        const int v0 = p * pv, v1 = min(nv, v0 + pv);
+        if (v1 > v0) {
+          mbar_arrive_expect_tx(&bars[p], (unsigned)(v1 - v0) * 16u);
+          bulk_load(data + v0, reinterpret_cast<const uint4*>(src) + v0, (unsigned)(v1 - v0) * 16u, &bars[p]);
+        }
+      }
+    }
+  } else {
+    T* d = reinterpret_cast<T*>(data);
+    for (int i = threadIdx.x; i < n; i += kThreads) d[i] = src[i];
+  }
+  for (int i = threadIdx.x; i < kBins; i += kThreads) hist[i] = 0u;
+  if (threadIdx.x == 0) {
+    s_bin = 0;
+    s_above = 0u;
+    s_cnt = 0;
+  }
+  __syncthreads();
+
+  // 2. Radix select: find the lower edge `lo` of the bin holding the k-th largest composite, refining until the
+  //    composites at or above it fit the candidate buffer.
+  const unsigned kk0 = (unsigned)min(a.k, n);
+  u64 lo = 0;
+  bool ok = true;
+  if (n <= kCap) {
+    if constexpr (kBulk) {
+#pragma unroll
+      for (int p = 0; p < kPieces; ++p)
+        if (min(nv, p * pv + pv) > p * pv) ok = mbar_wait(&bars[p], 0) && ok;
+    }
+  } else {
+    u64 prefix = 0;
+    unsigned kk = kk0, above_total = 0;
+    for (int L = 0; L < kLevels; ++L) {
+      const int sh = level_shift(L), w = level_width(L);
+      const unsigned mask = (1u << w) - 1u;
+      for (int p = 0; p < kPieces; ++p) {
+        const int v0 = p * pv, v1 = min(nv, v0 + pv);
+        if (v1 <= v0) continue;
+        if constexpr (kBulk) {
+          if (L == 0) ok = mbar_wait(&bars[p], 0) && ok;
+        }
+        for (int i = v0 + threadIdx.x; i < v1; i += kThreads) {
+          unsigned key[V];
+          keys16(data[i], key, tag);
+#pragma unroll
+          for (int e = 0; e < V; ++e) {
+            const int idx = i * V + e;
+            if (idx < n) {
+              const u64 c = composite(key[e], base_idx + (unsigned)idx);
+              if (L == 0 || (c >> (sh + w)) == prefix) atomicAdd(&hist[(unsigned)(c >> sh) & mask], 1u);
+            }
+          }
+        }
+      }
+      __syncthreads();
+      // Boundary bin: thread t owns bins [t * per, (t + 1) * per); scan from the top.
+      const int per = (1 << w) / kThreads;
+      unsigned mine = 0;
+      for (int b = 0; b < per; ++b) mine += hist[threadIdx.x * per + b];
+      unsigned run = block_suffix_excl(mine, warp_tot);
+      for (int b = per - 1; b >= 0; --b) {
+        const unsigned h = hist[threadIdx.x * per + b];
+        if (run < kk && run + h >= kk) {
+          s_bin = threadIdx.x * per + b;
+          s_above = run;
+        }
+        run += h;
+      }
+      __syncthreads();
+      const int bin = s_bin;
+      const unsigned above = s_above, inbin = hist[bin];
+      const u64 next = (prefix << w) | (u64)bin;
+      lo = next << sh;
+      if (above_total + above + inbin <= (unsigned)kCap || L == kLevels - 1) break;
+      above_total += above;
+      kk -= above;
+      prefix = next;
+      __syncthreads();  // every thread has read hist[bin]
+      for (int i = threadIdx.x; i < kBins; i += kThreads) hist[i] = 0u;
+      __syncthreads();
+    }
+  }
+  if (!ok) atomicOr(&g_topk_status, CKB_STATUS_TIMEOUT);
+  __syncthreads();  // the histogram is dead from here: the candidate buffer reuses it
+
+  // 3. Collect the composites >= lo (warp-aggregated appends).
+  const int lane = threadIdx.x & 31;
+  for (int i0 = 0; i0 < nv; i0 += kThreads) {
+    const int i = i0 + threadIdx.x;
+    unsigned key[V];
+    if (i < nv) keys16(data[i], key, tag);
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const int idx = i * V + e;
+      u64 c = 0;
+      bool take = false;
+      if (i < nv && idx < n) {
+        c = composite(key[e], base_idx + (unsigned)idx);
+        take = c >= lo;
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, take);
+      if (m) {
+        int at = 0;
+        if (lane == 0) at = atomicAdd(&s_cnt, __popc(m));
+        at = __shfl_sync(0xffffffffu, at, 0);
+        if (take) {
+          const int pos = at + __popc(m & ((1u << lane) - 1u));
+          if (pos < kCap) cand[pos] = c;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int cnt = min(s_cnt, kCap);
+
+  // 4. The chunk's top k, sorted, into top[0, k) (zero padded when the chunk has fewer than k elements).
+  if (cnt <= kSortMax) {
+    if (threadIdx.x < 32) {
+      u64 v[kSortMax / 32];
+#pragma unroll
+      for (int p = 0; p < kSortMax / 32; ++p) {
+        const int e = lane * (kSortMax / 32) + p;
+        v[p] = e < cnt ? cand[e] : 0ull;
+      }
+      warp_sort_desc<kSortMax / 32>(v);
+#pragma unroll
+      for (int p = 0; p < kSortMax / 32; ++p) {
+        const int e = lane * (kSortMax / 32) + p;
+        if (e < a.k) top[e] = v[p];
+      }
+    }
+    for (int e = kSortMax + threadIdx.x; e < a.k; e += kThreads) top[e] = 0ull;
+  } else {
+    for (int i = threadIdx.x; i < cnt; i += kThreads) {
+      const u64 c = cand[i];
+      int rank = 0;
+      for (int j = 0; j < cnt; ++j) rank += cand[j] > c;
+      if (rank < a.k) top[rank] = c;
+    }
+    for (int e = cnt + threadIdx.x; e < a.k; e += kThreads) top[e] = 0ull;
+  }
+  __syncthreads();
+
+  // 5. Output, or the multi-chunk merge by the row's last CTA.
+  if (nchunks == 1) {
+    for (int j = threadIdx.x; j < a.k; j += kThreads) emit<T>(a, row, j, top[j]);
+    return;
+  }
+  u64* wr = a.work + row * (long long)nchunks * a.k;
+  for (int j = threadIdx.x; j < a.k; j += kThreads) wr[(long long)blockIdx.x * a.k + j] = top[j];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[row], 1u) == (unsigned)nchunks - 1u;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int total = nchunks * a.k;
+  u64* lists = reinterpret_cast<u64*>(smem_raw);
+  for (int i = threadIdx.x; i < total; i += kThreads) lists[i] = __ldcg(wr + i);
+  __syncthreads();
+  for (int i = threadIdx.x; i < total; i += kThreads) {
+    const u64 c = lists[i];
+    if (c == 0ull) continue;
+    const int own = i / a.k;
+    int rank = i - own * a.k;
+    for (int l = 0; l < nchunks && rank < a.k; ++l)
+      if (l != own) rank += count_greater(lists + l * a.k, a.k, c);
+    if (rank < a.k) emit<T>(a, row, rank, c);
+  }
+  if (threadIdx.x == 0) a.counters[row] = 0u;
+}
+
+// Merge of nlists sorted composite lists per row, lists laid out [nlists][rows][k] (an all-gather's output); one
+// CTA per row writes the top k values and indices.
+template <typename T>
+__global__ void __launch_bounds__(256) topk_merge(const u64* __restrict__ lists, int nlists, long long rows, int k,
+                                                  T* __restrict__ values, long long* __restrict__ indices) {
+  extern __shared__ __align__(16) u64 sl[];
+  const long long row = blockIdx.x;
+  const int total = nlists * k;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int l = i / k, j = i - l * k;
+    sl[i] = __ldg(lists + ((long long)l * rows + row) * k + j);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const u64 c = sl[i];
+    if (c == 0ull) continue;
+    const int own = i / k;
+    int rank = i - own * k;
+    for (int l = 0; l < nlists && rank < k; ++l)
+      if (l != own) rank += count_greater(sl + l * k, k, c);
+    if (rank < k) {
+      values[row * k + rank] = decode_value<T>(c);
+      indices[row * k + rank] = decode_index(c);
+    }
+  }
+}
+
+// Columns per CTA: the fewest chunks whose staged bytes fit kChunkBytes, raised (down to min_chunk columns, up to
+// kGrowChunks chunks so the last CTA's merge stays short) until the grid holds at least three CTAs per SM; a multiple
+// of 16 columns so every chunk starts 16-byte aligned.
+constexpr long long kGrowChunks = 32;
+
+long long plan_chunk(long long rows, long long cols, int elem, int min_chunk) {
+  if (rows <= 0 || cols <= 0) return cols > 0 ? cols : 1;
+  const long long max_elems = kChunkBytes / elem;
+  long long nchunks = (cols + max_elems - 1) / max_elems;
+  const long long target = 3LL * device_sm_count();
+  if (min_chunk < 1024) min_chunk = 1024;
+  while (rows * nchunks < target && nchunks < kGrowChunks && (cols + nchunks) / (nchunks + 1) >= min_chunk)
+    ++nchunks;
+  if (nchunks <= 1) return cols;
+  long long chunk = (cols + nchunks - 1) / nchunks;
+  chunk = (chunk + 15) / 16 * 16;
+  return chunk;
+}
+
+int data_bytes_for(long long chunk, int elem, int nchunks, int k) {
+  long long b = chunk * elem;
+  if (b < (long long)k * 8) b = (long long)k * 8;
+  if (nchunks > 1 && b < (long long)nchunks * k * 8) b = (long long)nchunks * k * 8;
+  return (int)((b + 127) / 128 * 128);
+}
+
+template <typename T>
+int start_chunk(const ChunkArgs& base, long long rows, long long cols, long long chunk, cudaStream_t s) {
+  const int elem = (int)sizeof(T);
+  const long long nchunks = (cols + chunk - 1) / chunk;
+  ChunkArgs a = base;
+  a.cols = (int)cols;
+  a.chunk = (int)chunk;
+  a.data_bytes = data_bytes_for(chunk, elem, (int)nchunks, a.k);
+  if (a.data_bytes > kMaxDataBytes) return -1;
+  const int smem = a.data_bytes + kBins * 4;
+  const bool bulk = aligned16(a.x) && (cols * elem) % 16 == 0 && (chunk * elem) % 16 == 0;
+  const dim3 grid((unsigned)nchunks, (unsigned)rows);
+  if (bulk) {
+    auto kern = topk_chunk<T, true>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return (int)cudaGetLastError();
+    kern<<<grid, kThreads, smem, s>>>(a);
+  } else {
+    auto kern = topk_chunk<T, false>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return (int)cudaGetLastError();
+    kern<<<grid, kThreads, smem, s>>>(a);
+  }
+  return (int)cudaGetLastError();
+}
+
+// The reference's argument checks (topk/kernel.cu:551-554) plus this library's chunk staging limit.
+bool bad_args(long long rows, long long cols, int k, long long chunk, int elem) {
+  if (k > cols || k > kMaxK || cols > INT_MAX / 2 || rows > 65535 || chunk <= 0) return true;
+  const long long nchunks = (cols + chunk - 1) / chunk;
+  if (nchunks > 1 && (chunk % 4 || nchunks * k > INT_MAX / 2)) return true;
+  if (chunk > cols) chunk = cols;
+  return data_bytes_for(chunk, elem, (int)nchunks, k) > kMaxDataBytes;
+}
+
+}  // namespace
+}  // namespace ckb
+
+using namespace ckb;
+
+// Replaces the reference's top-k `plan` (topk/kernel.cu:520-547): the columns per CTA for a rows x cols launch
+// (dtype 0 fp32, 1 bf16). `threads` and `depth` are the reference's kernel knobs and do not change the B200 plan;
+// min_chunk is a lower bound on the chunk when a row is split to fill the GPU. A row's chunk count is
+// ceil(cols / chunk); the workspace launch() needs is rows * chunks * k int64 values.
+CKB_EXPORT long long plan(long long rows, long long cols, int dtype, int threads, int depth, int min_chunk) {
+  (void)threads;
+  (void)depth;
+  return plan_chunk(rows, cols, dtype == kBF16 ? 2 : 4, min_chunk);
+}
+
+// Replaces the reference's top-k `launch` (topk/kernel.cu:549-570): same arguments, checks and return codes. work is
+// int64 [rows * nchunks * k] (unused with one chunk), counters int32 [rows] zeroed once and left zeroed by the kernel.
+// `chunk` must come from plan() (or be small enough for the shared-memory staging; larger gives -1).
+CKB_EXPORT int launch(const void* x, void* values, void* indices, void* work, void* counters, long long rows,
+                      long long cols, int k, int dtype, int threads, int depth, long long chunk,
+                      cudaStream_t stream) {
+  if (rows <= 0 || k <= 0) return 0;
+  if (threads != 128 && threads != 256 && threads != 512) return -1;
+  if (depth != 2 && depth != 4 && depth != 8) return -1;
+  const int elem = dtype == kBF16 ? 2 : 4;
+  if (bad_args(rows, cols, k, chunk, elem)) return -1;
+  if (chunk > cols) chunk = cols;
+  ChunkArgs a{x, values, (long long*)indices, nullptr, (u64*)work, (unsigned*)counters, 0, 0, 0, k, 0, 0};
+  if (dtype == kF32) return start_chunk<float>(a, rows, cols, chunk, stream);
+  if (dtype == kBF16) return start_chunk<__nv_bfloat16>(a, rows, cols, chunk, stream);
+  return -1;
+}
+
+// Top-k of a column shard for the vocab-sharded variant (no counterpart in the reference): x is [rows, cols] holding
+// global columns [col_offset, col_offset + cols); lists receives [rows, k] sorted composites (uint64, zero padded)
+// carrying global indices, ready for an all-gather and ckb_topk_merge_launch. work/counters/chunk as in launch().
+CKB_EXPORT int ckb_topk_shard_launch(const void* x, unsigned long long* lists, void* work, void* counters,
+                                     long long rows, long long cols, long long col_offset, int k, int dtype,
+                                     long long chunk, cudaStream_t stream) {
+  if (rows <= 0 || k <= 0) return 0;
+  const int elem = dtype == kBF16 ? 2 : 4;
+  if (col_offset < 0 || col_offset + cols > INT_MAX / 2 || bad_args(rows, cols, k, chunk, elem)) return -1;
+  if (chunk > cols) chunk = cols;
+  ChunkArgs a{x, nullptr, nullptr, lists, (u64*)work, (unsigned*)counters, col_offset, 0, 0, k, 0, 1};
+  if (dtype == kF32) return start_chunk<float>(a, rows, cols, chunk, stream);
+  if (dtype == kBF16) return start_chunk<__nv_bfloat16>(a, rows, cols, chunk, stream);
+  return -1;
+}
+
+// Final merge of the vocab-sharded variant (no counterpart in the reference): lists [nlists][rows][k] of sorted
+// composites (one list per shard) -> values [rows, k] in the dtype (0 fp32, 1 bf16) and int64 indices [rows, k].
+CKB_EXPORT int ckb_topk_merge_launch(const unsigned long long* lists, int nlists, void* values, void* indices,
+                                     long long rows, int k, int dtype, cudaStream_t stream) {
+  if (rows <= 0 || k <= 0) return 0;
+  if (nlists <= 0 || k > kMaxK || rows > INT_MAX) return -1;
+  const long long smem = (long long)nlists * k * 8;
+  if (smem > kMaxDataBytes) return -1;
+  if (dtype == kF32) {
+    if (cudaFuncSetAttribute(topk_merge<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return (int)cudaGetLastError();
+    topk_merge<float><<<(unsigned)rows, 256, (size_t)smem, stream>>>((const u64*)lists, nlists, rows, k,
+                                                                     (float*)values, (long long*)indices);
+  } else if (dtype == kBF16) {
+    if (cudaFuncSetAttribute(topk_merge<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return (int)cudaGetLastError();
+    topk_merge<__nv_bfloat16><<<(unsigned)rows, 256, (size_t)smem, stream>>>(
+        (const u64*)lists, nlists, rows, k, (__nv_bfloat16*)values, (long long*)indices);
+  } else {
+    return -1;
+  }
+  return (int)cudaGetLastError();
+}
+
+// Status of the bounded waits in this library's kernels since the last reset: 0, or 1 when a bulk-copy wait gave up.
+// Synchronises with the device; reset != 0 clears the word.
+CKB_EXPORT int ckb_topk_status(int reset) {
+  unsigned v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_topk_status, sizeof(v));
+  if (e != cudaSuccess) return -(int)e;
+  if (reset) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(g_topk_status, &zero, sizeof(zero));
+    if (e != cudaSuccess) return -(int)e;
+  }
+  return (int)v;
+}

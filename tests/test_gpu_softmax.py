@@ -1,0 +1,106 @@
+"""Softmax parity on the GPU against the fp64 oracle (the reference's torch.softmax, softmax/baseline.py:5-6,13).
+
+Tolerance: fp32 outputs within 1e-6 relative of fp64 elementwise; bf16 outputs within 1 bf16 ulp of the fp64 result
+rounded to bf16. NaN exactly where the oracle has NaN (a row with +inf or NaN is all NaN, as in torch).
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from ckb200 import softmax, workloads
+from helpers import assert_rel, assert_ulp, guarded_empty, misaligned_copy, ref_lib
+from oracle import softmax as orc
+
+pytestmark = pytest.mark.gpu
+REL = 1e-6
+
+
+def _check(x, y, what):
+    want = orc.softmax_f64(x)
+    if x.dtype == torch.float32:
+        assert_rel(y, want, REL, what)
+    else:
+        assert_ulp(y.cpu(), want.to(torch.bfloat16), torch.bfloat16, 1, what)
+
+
+def test_config1_4096x8192():
+    x = workloads.softmax_4096x8192()["x"]
+    _check(x, softmax.run({"x": x.cuda()})["y"], "4096x8192")
+
+
+def test_config4_long_rows_cluster_path():
+    x = workloads.softmax_256x262144()["x"]
+    _check(x, softmax.run({"x": x.cuda()})["y"], "256x262144")
+
+
+def test_config4_short_rows():
+    x = workloads.softmax_262144x128()["x"]
+    _check(x, softmax.run({"x": x.cuda()})["y"], "262144x128")
+
+
+# Column counts that reach every path: group (G = 4, 8, 16, 32), block, cluster (several cluster sizes), and the
+# stream fallback (cols not a multiple of the vector).
+COLS = [1, 4, 12, 16, 32, 100, 128, 256, 512, 1024, 2048, 8192, 16384, 20000, 65536, 100000, 262144, 1048576,
+        13, 1001, 40001]
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("cols", COLS)
+def test_shapes(dtype, cols):
+    rows = 3 if cols >= 65536 else 37
+    g = torch.Generator().manual_seed(cols)
+    x = (torch.randn(rows, cols, generator=g) * 3).to(dtype)
+    y, check = guarded_empty((rows, cols), dtype)
+    softmax.softmax(x.cuda(), out=y)
+    torch.cuda.synchronize()
+    check()
+    _check(x, y, f"{rows}x{cols} {dtype}")
+
+
+@pytest.mark.parametrize("cols", [128, 8192, 262144])
+def test_misaligned(cols):
+    x = torch.randn(3, cols, generator=torch.Generator().manual_seed(1))
+    xd = misaligned_copy(x.cuda())
+    _check(x, softmax.softmax(xd), f"misaligned {cols}")
+
+
+@pytest.mark.parametrize("cols", [128, 8192, 262144])
+def test_special_values(cols):
+    x = torch.randn(5, cols, generator=torch.Generator().manual_seed(2))
+    x[0, 3] = float("-inf")
+    x[1, :] = float("-inf")
+    x[2, 5] = float("inf")
+    x[3, 9] = float("nan")
+    x[4, :] = 0.0
+    _check(x, softmax.softmax(x.cuda()), f"special {cols}")
+
+
+def test_three_dims():
+    x = torch.randn(4, 5, 96, generator=torch.Generator().manual_seed(3))
+    _check(x, softmax.run({"x": x.cuda()})["y"], "3-D")
+
+
+def test_no_bulk_wait_timed_out():
+    lib = ctypes.CDLL(softmax._native._build.lib_path("softmax"))
+    assert lib.ckb_softmax_status(1) == 0
+
+
+def test_matches_reference_kernel():
+    lib = ref_lib("softmax")
+    if lib is None:
+        pytest.skip("oracle/_ref not built")
+    lib.launch.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_longlong, ctypes.c_int,
+                           ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    for rows, cols in ((64, 8192), (8, 262144), (1024, 128)):
+        x = (torch.randn(rows, cols, generator=torch.Generator().manual_seed(rows)) * 2).cuda()
+        ref = torch.empty_like(x)
+        assert lib.launch(x.data_ptr(), ref.data_ptr(), rows, cols, 0, 256, 1024,
+                          torch.cuda.current_stream().cuda_stream) == 0
+        got = softmax.softmax(x)
+        want = orc.softmax_f64(x.cpu())
+        assert_rel(got, want, REL, "ours")
+        # the reference kernel against the same oracle, for the record (its division-based path is as accurate)
+        assert_rel(ref, want, 2 * REL, "reference kernel")

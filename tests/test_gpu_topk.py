@@ -1,0 +1,136 @@
+"""Top-k parity on the GPU against the exact CPU oracle (composite order of topk/kernel.cu:1-3,56-60): values bit
+for bit and indices equal, descending, ties by lower index."""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from ckb200 import topk, workloads
+from helpers import bits_equal, misaligned_copy, ref_lib
+from oracle import topk as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _check(x, k, values, indices, what=""):
+    wv, wi = orc.topk(x.cpu(), k)
+    assert torch.equal(indices.cpu(), wi), f"{what}: indices differ"
+    assert bits_equal(values, wv), f"{what}: values differ"
+
+
+def test_config_512x151936():
+    x = workloads.topk_512x151936()["x"]
+    out = topk.run({"x": x.cuda()})
+    _check(x, 50, out["values"], out["indices"], "config")
+
+
+def test_config_bf16():
+    x = workloads.topk_512x151936(scale=4)["x"].to(torch.bfloat16)
+    out = topk.run({"x": x.cuda()})
+    _check(x, 50, out["values"], out["indices"], "config bf16")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rows,cols,k", [(1, 128256, 50), (64, 151936, 50), (512, 32000, 50), (3, 50, 50),
+                                         (5, 1000, 1), (2, 4096, 512), (7, 2049, 64), (1, 1000003, 50),
+                                         (4, 33, 33), (300, 2048, 17), (2, 262144, 512)])
+def test_shapes(dtype, rows, cols, k):
+    g = torch.Generator().manual_seed(rows * 7 + cols)
+    x = (torch.randn(rows, cols, generator=g) * 3).to(dtype)
+    vv, ii = topk.topk(x.cuda(), k)
+    _check(x, k, vv, ii, f"{rows}x{cols} k={k} {dtype}")
+
+
+@pytest.mark.parametrize("cols", [151936, 5000, 1999])
+def test_ties_take_lower_index(cols):
+    """Few distinct values: every selection boundary is a tie (torch.topk on CPU would not break these by index)."""
+    g = torch.Generator().manual_seed(cols)
+    x = torch.randint(-3, 4, (6, cols), generator=g).float()
+    vv, ii = topk.topk(x.cuda(), 50)
+    _check(x, 50, vv, ii, "ties")
+
+
+def test_all_equal_rows():
+    x = torch.full((3, 100000), 1.5)
+    x[1] = -0.0
+    x[2, ::2] = 0.0  # +0 and -0 are different keys: +0 ranks above -0
+    vv, ii = topk.topk(x.cuda(), 50)
+    _check(x, 50, vv, ii, "equal")
+
+
+def test_special_values():
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(4, 20000, generator=g)
+    x[0, 100] = float("inf")
+    x[0, 200] = float("-inf")
+    x[1, 5] = float("nan")
+    x[1, 6] = -float("nan")
+    x[2, :] = float("-inf")
+    x[3, 1000:1060] = float("inf")
+    vv, ii = topk.topk(x.cuda(), 50)
+    _check(x, 50, vv, ii, "special")
+
+
+def test_misaligned_and_odd_cols_use_scalar_staging():
+    x = torch.randn(9, 30001, generator=torch.Generator().manual_seed(3))
+    xd = misaligned_copy(x.cuda())
+    vv, ii = topk.topk(xd, 50)
+    _check(x, 50, vv, ii, "misaligned")
+
+
+def test_repeated_calls_reuse_workspace_and_counters():
+    x = workloads.topk_512x151936(scale=8)["x"].cuda()
+    first = topk.topk(x, 50)
+    for _ in range(3):
+        again = topk.topk(x, 50)
+        assert torch.equal(first[1], again[1]) and bits_equal(first[0], again[0])
+    assert int(topk._row_counters(x.device, x.shape[0])[: x.shape[0]].abs().sum()) == 0
+
+
+def test_shard_and_merge_equal_full_topk():
+    """The vocab-sharded variant's two kernels on one GPU: 8 column shards -> lists -> merge == top-k of the row."""
+    x = workloads.topk_512x151936(scale=4)["x"]
+    xd = x.cuda()
+    shards = 8
+    bounds = np.linspace(0, x.shape[1], shards + 1).astype(int)
+    lists = torch.stack([topk.shard_lists(xd[:, a:b].contiguous(), int(a), 50) for a, b in zip(bounds, bounds[1:])])
+    want_lists = torch.stack([orc.shard_lists(x[:, a:b], int(a), 50) for a, b in zip(bounds, bounds[1:])])
+    assert torch.equal(lists.cpu(), want_lists)
+    vv, ii = topk.merge_lists(lists, torch.float32, 50)
+    _check(x, 50, vv, ii, "shard+merge")
+
+
+def test_no_bulk_wait_timed_out():
+    lib = ctypes.CDLL(topk._native._build.lib_path("topk"))
+    assert lib.ckb_topk_status(1) == 0
+
+
+def test_matches_reference_kernel():
+    lib = ref_lib("topk")
+    if lib is None:
+        pytest.skip("oracle/_ref not built")
+    lib.plan.argtypes = [ctypes.c_longlong, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    lib.plan.restype = ctypes.c_longlong
+    lib.launch.argtypes = [ctypes.c_void_p] * 5 + [ctypes.c_longlong, ctypes.c_longlong, ctypes.c_int, ctypes.c_int,
+                                                   ctypes.c_int, ctypes.c_int, ctypes.c_longlong, ctypes.c_void_p]
+    x = workloads.topk_512x151936(scale=8)["x"].cuda()
+    rows, cols = x.shape
+    chunk = lib.plan(rows, cols, 0, 256, 4, 2048)
+    nch = -(-cols // chunk)
+    work = torch.empty(max(1, rows * nch * 50), dtype=torch.int64, device="cuda")
+    counters = torch.zeros(4096, dtype=torch.int32, device="cuda")
+    rv = torch.empty(rows, 50, device="cuda")
+    ri = torch.empty(rows, 50, dtype=torch.int64, device="cuda")
+    assert lib.launch(x.data_ptr(), rv.data_ptr(), ri.data_ptr(), work.data_ptr(), counters.data_ptr(), rows, cols,
+                      50, 0, 256, 4, chunk, torch.cuda.current_stream().cuda_stream) == 0
+    vv, ii = topk.topk(x, 50)
+    assert torch.equal(ii, ri) and bits_equal(vv, rv)
+
+
+def test_bad_arguments_raise():
+    with pytest.raises(ValueError):
+        topk.run({"x": torch.zeros(2, 49, device="cuda")})
+    with pytest.raises(ValueError):
+        topk.run({"x": torch.zeros(2, 100, dtype=torch.float16, device="cuda")})

@@ -1,0 +1,164 @@
+"""The oracle against the reference: golden fixtures made by the reference's own code (tests/golden/make_golden.py)
+plus known-answer cases. CPU only."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import rmsnorm as orms
+from oracle import rope as orope
+from oracle import softmax as osm
+from oracle import topk as otk
+from oracle.numerics import f32_to_bf16_bits, round_to, to_f32, ulp_distance
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _load(name):
+    path = os.path.join(GOLDEN, name)
+    if not os.path.exists(path):
+        pytest.skip(f"{name} not generated yet (tests/golden/make_golden.py --gpu on a B200)")
+    return np.load(path)
+
+
+def _t16(bits, dtype):
+    return torch.from_numpy(np.ascontiguousarray(bits)).view(dtype)
+
+
+# --------------------------------------------------------------------------------------------------- numerics ----
+def test_bf16_rounding_matches_torch():
+    g = torch.Generator().manual_seed(0)
+    f = torch.cat([torch.randn(100000, generator=g) * 10 ** torch.randint(-30, 30, (100000,), generator=g).float(),
+                   torch.tensor([0.0, -0.0, float("inf"), -float("inf"), 3.3895e38, 1e-40, -1e-45])])
+    ours = f32_to_bf16_bits(f.numpy())
+    want = f.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(ours, want)
+
+
+def test_ulp_distance():
+    a = np.array([1.0, 1.0, -1.0, 0.0], dtype=np.float32)
+    b = np.array([1.0, 1.0078125, -1.0078125, -0.0], dtype=np.float32)
+    assert ulp_distance(a, b, torch.bfloat16).tolist() == [0, 1, 1, 0]
+
+
+# ---------------------------------------------------------------------------------------------------- softmax ----
+def test_softmax_oracle_matches_reference_baseline():
+    z = _load("softmax.npz")
+    for i in range(4):
+        x = torch.from_numpy(z[f"x{i}"])
+        assert np.array_equal(osm.softmax_f64(x).numpy(), z[f"y64_{i}"], equal_nan=True)
+        assert np.array_equal(osm.softmax_cpu(x).numpy(), z[f"y32_{i}"], equal_nan=True)
+        xb = _t16(z[f"xbf16_{i}"], torch.bfloat16)
+        yb = osm.softmax_cpu(xb)
+        assert np.array_equal(yb.view(torch.int16).numpy(), z[f"ybf16_{i}"])
+
+
+def test_softmax_known_answers():
+    x = torch.tensor([[0.0, 0.0], [1.0, float("-inf")], [1.0, float("inf")], [float("nan"), 0.0]])
+    y = osm.softmax_f64(x)
+    assert y[0].tolist() == [0.5, 0.5]
+    assert y[1].tolist() == [1.0, 0.0]
+    assert torch.isnan(y[2]).all() and torch.isnan(y[3]).all()
+
+
+# ---------------------------------------------------------------------------------------------------- rmsnorm ----
+def test_rmsnorm_oracle_matches_reference_kernel():
+    z = _load("rmsnorm.npz")
+    for i in range(4):
+        dt = torch.bfloat16 if int(z[f"dtype{i}"]) == 1 else torch.float16
+        x = _t16(z[f"x{i}"], dt)
+        want = _t16(z[f"y{i}"], dt)
+        got = orms.rmsnorm(x)
+        d = ulp_distance(to_f32(got), to_f32(want), dt)
+        assert d.max() <= 1
+        assert (d == 0).mean() > 0.99
+
+
+def test_rmsnorm_known_answers():
+    # rows of a constant c: mean(x^2) = c^2, inv = 1/|c| (exact for powers of two), y = sign(c)
+    x = torch.tensor([[2.0] * 8, [-4.0] * 8, [0.25] * 8], dtype=torch.bfloat16)
+    y = orms.rmsnorm(x, eps=0.0)
+    assert y.float().tolist() == [[1.0] * 8, [-1.0] * 8, [1.0] * 8]
+    w = torch.arange(8, dtype=torch.float32)
+    assert orms.rmsnorm(x, w, eps=0.0).float()[0].tolist() == list(range(8))
+    nan_row = orms.rmsnorm(torch.tensor([[1.0, float("nan")]], dtype=torch.float16))
+    assert torch.isnan(nan_row).all()
+
+
+def test_rmsnorm_inverse_rounding_is_the_references():
+    # inv is rounded to the dtype before the product (rmsnorm/kernel.cu:46): with x = [3, 0, 0, 0],
+    # inv = 1/sqrt(9/4) = 0.6667 -> bf16 0.66796875 and y0 = bf16(3 * 0.66796875) = 2.0 exactly
+    x = torch.tensor([[3.0, 0.0, 0.0, 0.0]], dtype=torch.bfloat16)
+    assert orms.rmsnorm(x, eps=0.0).float()[0, 0].item() == 2.0
+
+
+# ------------------------------------------------------------------------------------------------------- rope ----
+def test_rope_oracle_matches_reference_kernel_bit_for_bit():
+    z = _load("rope.npz")
+    for i in range(4):
+        qk = torch.bfloat16 if int(z[f"qk{i}"]) == 1 else torch.float16
+        cd = {0: torch.float32, 1: torch.bfloat16, 2: torch.float16}[int(z[f"cache{i}"])]
+        q, k = _t16(z[f"q{i}"], qk), _t16(z[f"k{i}"], qk)
+        cos = torch.from_numpy(z[f"cos{i}"]) if cd == torch.float32 else _t16(z[f"cos{i}"], cd)
+        sin = torch.from_numpy(z[f"sin{i}"]) if cd == torch.float32 else _t16(z[f"sin{i}"], cd)
+        ids = torch.from_numpy(z[f"ids{i}"])
+        qo, ko = orope.rope(q, k, cos, sin, ids)
+        assert np.array_equal(qo.view(torch.int16).numpy(), z[f"qo{i}"])
+        assert np.array_equal(ko.view(torch.int16).numpy(), z[f"ko{i}"])
+
+
+def test_rope_known_answers():
+    # position 0: cos = 1, sin = 0 -> identity; a quarter turn swaps the halves with a sign
+    q = torch.tensor([[[[1.0, 2.0, 3.0, 4.0]]]], dtype=torch.bfloat16)
+    cos = torch.tensor([[1.0, 1.0, 1.0, 1.0], [0.0, 0.0, 0.0, 0.0]])
+    sin = torch.tensor([[0.0, 0.0, 0.0, 0.0], [1.0, 1.0, 1.0, 1.0]])
+    qo, _ = orope.rope(q, q, cos, sin, torch.tensor([[0]]))
+    assert qo.float().flatten().tolist() == [1.0, 2.0, 3.0, 4.0]
+    qo, _ = orope.rope(q, q, cos, sin, torch.tensor([[1]]))
+    assert qo.float().flatten().tolist() == [-3.0, -4.0, 1.0, 2.0]
+
+
+def test_rope_cpu_baseline_agrees_with_oracle():
+    g = torch.Generator().manual_seed(1)
+    q = torch.randn(2, 8, 4, 64, generator=g).to(torch.bfloat16)
+    k = torch.randn(2, 8, 2, 64, generator=g).to(torch.bfloat16)
+    cos, sin = orope.cos_sin_cache(1e4, 64, 16)
+    ids = torch.randint(0, 16, (2, 8), generator=g)
+    a = orope.rope(q, k, cos, sin, ids)
+    b = orope.rope_cpu(q, k, cos, sin, ids)
+    for x, y in zip(a, b):
+        assert ulp_distance(to_f32(x), to_f32(y), torch.bfloat16).max() <= 1
+
+
+# ------------------------------------------------------------------------------------------------------- topk ----
+def test_topk_oracle_matches_reference_kernel():
+    z = _load("topk.npz")
+    for i in range(4):
+        dt = torch.bfloat16 if int(z[f"dtype{i}"]) == 1 else torch.float32
+        x = _t16(z[f"x{i}"], dt) if dt == torch.bfloat16 else torch.from_numpy(z[f"x{i}"])
+        v, ix = otk.topk(x, 50)
+        assert np.array_equal(ix.numpy(), z[f"i{i}"])
+        vb = v.view(torch.int16).numpy() if dt == torch.bfloat16 else v.numpy().view(np.uint32)
+        want = z[f"v{i}"] if dt == torch.bfloat16 else z[f"v{i}"].view(np.uint32)
+        assert np.array_equal(vb, want)
+
+
+def test_topk_known_answers_ties_by_lower_index():
+    x = torch.tensor([[1.0, 3.0, 3.0, 2.0, 3.0]])
+    v, i = otk.topk(x, 3)
+    assert i.tolist() == [[1, 2, 4]] and v.tolist() == [[3.0, 3.0, 3.0]]
+    x = torch.tensor([[0.0, -0.0, float("nan"), float("inf"), -float("inf"), -float("nan")]])
+    _, i = otk.topk(x, 6)
+    assert i.tolist() == [[2, 3, 0, 1, 4, 5]]
+
+
+def test_topk_shard_merge_equals_full():
+    g = torch.Generator().manual_seed(3)
+    x = torch.randint(-20, 20, (5, 1003), generator=g).float()
+    bounds = [0, 100, 517, 1003]
+    lists = torch.stack([otk.shard_lists(x[:, a:b], a, 50) for a, b in zip(bounds, bounds[1:])])
+    v, i = otk.merge_lists(lists, torch.float32, 50)
+    wv, wi = otk.topk(x, 50)
+    assert torch.equal(i, wi) and torch.equal(v, wv)
