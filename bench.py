@@ -433,6 +433,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default=HEADLINE)
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-kernel sweep of the other configs")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--sweep-steps", type=int, default=300)
     ap.add_argument("--e2e-steps", type=int, default=20)
     args = ap.parse_args()
@@ -468,12 +469,12 @@ def main():
     }
     if args.workload == HEADLINE:
         line["e2e"] = e2e_rmsnorm(args.e2e_steps, 3, world)
-    if world == 1 and rank == 0:
+    if world == 1 and rank == 0 and not args.no_cpu:
         gbs_cpu, sample, threads = cpu_sample_rate(args.workload)
         line["cpu_baseline"] = {"value": round(gbs_cpu, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                                 "sample": sample}
-        if not args.no_sweep:
-            line["kernels"] = sweep(args, world)
+    if world == 1 and rank == 0 and not args.no_sweep:
+        line["kernels"] = sweep(args, world)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -1,4 +1,4 @@
-"""ctypes bindings of the four kernel libraries (the reference's own FFI style, e.g. rmsnorm/candidate.py:23-26).
+"""ctypes bindings of the four kernel libraries (the reference's own FFI style, e.g. rmsnorm/candidate.py:25-28).
 
 A library that is missing raises at first use: there is no CPU or PyTorch fallback for any op. Every binding takes
 plain pointers, sizes and the caller's CUDA stream, exactly as declared in include/ckb200_<op>.h.
@@ -69,7 +69,7 @@ def stream_of(t):
 
 def check(err):
     """The reference wrappers' error convention (rmsnorm/candidate.py:50-51, rope/candidate.py:55-56,
-    topk/candidate.py:92-93): any non-zero return, -1 for rejected arguments included, raises RuntimeError."""
+    topk/candidate.py:79-80): any non-zero return, -1 for rejected arguments included, raises RuntimeError."""
     if err:
         raise RuntimeError(f"kernel launch failed: CUDA error {err}")
 

@@ -1,7 +1,7 @@
 """In-tree build of the four kernel libraries for sm_100a.
 
 Each op compiles from csrc/<op>.cu into lib/<op>/libkernel.so, the layout the reference's Python wrappers load
-(`$CKOPT_BUILD_DIR/libkernel.so`, e.g. rmsnorm/candidate.py:23-24): pointing CKOPT_BUILD_DIR at lib/<op> makes the
+(`$CKOPT_BUILD_DIR/libkernel.so`, e.g. rmsnorm/candidate.py:25): pointing CKOPT_BUILD_DIR at lib/<op> makes the
 reference's own candidate.py drive these kernels. The CUDA runtime is linked statically (nvcc's default), so a
 library needs only the driver at run time.
 """

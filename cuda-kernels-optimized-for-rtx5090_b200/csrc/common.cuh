@@ -101,8 +101,8 @@ __device__ __forceinline__ void st_stream(void* p, const uint4& v) { __stcs(rein
 // ---------------------------------------------------------------------------------------------------------------
 // Warp reductions (butterfly: every lane ends with the same bits).
 // ---------------------------------------------------------------------------------------------------------------
-template <int WIDTH = 32>
-__device__ __forceinline__ float warp_sum(float v) {
+template <int WIDTH = 32, typename F = float>
+__device__ __forceinline__ F warp_sum(F v) {
 #pragma unroll
   for (int o = WIDTH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;

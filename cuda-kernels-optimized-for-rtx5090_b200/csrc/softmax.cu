@@ -12,8 +12,11 @@
 //     mbarriers so the max can start on the first piece), the CTAs exchange the max and then the sum through
 //     distributed shared memory, and each CTA normalises from shared memory. No copy is multicast;
 //   * stream path (unaligned pointers, cols not a multiple of the vector, or rows too long for the cluster slices):
-//     one block per row with an online max/sum, then a second read of the row (L2-resident) to normalise.
-// exp is CUDA's expf; the normalisation multiplies by the correctly rounded reciprocal of the row sum.
+//     one block per row reading the row three times (max, sum, normalise; the later reads mostly from L2).
+// Accuracy (fp32 outputs within 1e-6 relative of an fp64 softmax, elementwise): exp(x - max) uses CUDA's expf on the
+// fp32 difference and folds the difference's rounding error back in (TwoSum), each thread sums its exponentials
+// pairwise per 16-byte vector into an fp64 accumulator and the cross-thread reductions run in fp64; the output is
+// e * (float)(1 / sum).
 #include "ckb200_softmax.h"
 #include "common.cuh"
 
@@ -34,6 +37,31 @@ namespace {
 template <typename T>
 __device__ __forceinline__ void store16(T* p, const float (&f)[VecN<T>::N]) {
   st_stream(p, pack16(f, p));
+}
+
+// exp(x - m) for m >= x. The fp32 difference d carries a rounding error of up to half an ulp of |d| (relative error
+// |d| * 2^-25 after exp, over 1e-6 once |d| > 32); TwoSum recovers that error lo exactly and exp(d + lo) is taken
+// as exp(d) * (1 + lo). A zero or NaN exponential (x = -inf, or an inf/NaN row) is left as it is.
+__device__ __forceinline__ float exp_shifted(float x, float m) {
+  const float d = x - m;
+  const float bv = d - x;
+  const float lo = (x - (d - bv)) + (-m - bv);
+  const float e = expf(d);
+  return e > 0.0f ? fmaf(e, lo, e) : e;
+}
+
+// Pairwise sum of the values of one 16-byte vector.
+__device__ __forceinline__ float vec_sum(const float (&f)[4]) { return (f[0] + f[1]) + (f[2] + f[3]); }
+__device__ __forceinline__ float vec_sum(const float (&f)[8]) {
+  return ((f[0] + f[1]) + (f[2] + f[3])) + ((f[4] + f[5]) + (f[6] + f[7]));
+}
+
+// In place: f = exp(f - m); returns their pairwise sum.
+template <int V>
+__device__ __forceinline__ float exp_vec(float (&f)[V], float m) {
+#pragma unroll
+  for (int j = 0; j < V; ++j) f[j] = exp_shifted(f[j], m);
+  return vec_sum(f);
 }
 
 // ------------------------------------------------------------------------------------------------ group path ----
@@ -66,18 +94,12 @@ __global__ void __launch_bounds__(256) sm_group(const T* __restrict__ x, T* __re
       for (int j = 0; j < V; ++j) m = fmaxf(m, v[k][j]);
     }
   m = warp_max<G>(m);
-  float s = 0.0f;
+  double s = 0.0;
 #pragma unroll
   for (int k = 0; k < NV; ++k)
-    if (in[k]) {
-#pragma unroll
-      for (int j = 0; j < V; ++j) {
-        v[k][j] = expf(v[k][j] - m);
-        s += v[k][j];
-      }
-    }
+    if (in[k]) s += (double)exp_vec(v[k], m);
   s = warp_sum<G>(s);
-  const float inv = 1.0f / s;
+  const float inv = (float)(1.0 / s);
 #pragma unroll
   for (int k = 0; k < NV; ++k)
     if (in[k]) {
@@ -92,7 +114,8 @@ __global__ void __launch_bounds__(256) sm_group(const T* __restrict__ x, T* __re
 template <typename T, int NV>
 __global__ void __launch_bounds__(NV >= 8 ? 512 : 1024) sm_block(const T* __restrict__ x, T* __restrict__ y, int cols) {
   constexpr int V = VecN<T>::N;
-  __shared__ float red_m[32], red_s[32];
+  __shared__ float red_m[32];
+  __shared__ double red_s[32];
   const int nvec = cols / V;
   const T* xr = x + (long long)blockIdx.x * cols;
   T* yr = y + (long long)blockIdx.x * cols;
@@ -118,22 +141,16 @@ __global__ void __launch_bounds__(NV >= 8 ? 512 : 1024) sm_block(const T* __rest
   __syncthreads();
   m = red_m[0];
   for (int i = 1; i < warps; ++i) m = fmaxf(m, red_m[i]);
-  float s = 0.0f;
+  double s = 0.0;
 #pragma unroll
   for (int k = 0; k < NV; ++k)
-    if (in[k]) {
-#pragma unroll
-      for (int j = 0; j < V; ++j) {
-        v[k][j] = expf(v[k][j] - m);
-        s += v[k][j];
-      }
-    }
+    if (in[k]) s += (double)exp_vec(v[k], m);
   s = warp_sum(s);
   if (lane == 0) red_s[warp] = s;
   __syncthreads();
-  s = 0.0f;
+  s = 0.0;
   for (int i = 0; i < warps; ++i) s += red_s[i];
-  const float inv = 1.0f / s;
+  const float inv = (float)(1.0 / s);
 #pragma unroll
   for (int k = 0; k < NV; ++k)
     if (in[k]) {
@@ -150,15 +167,23 @@ constexpr int kPieces = 4;  // bulk copies (and mbarriers) per slice
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
-// Block-wide fold of one value per thread through `red` (32 slots); every thread gets the same result.
-template <bool kMax>
-__device__ __forceinline__ float block_fold(float v, float* red) {
-  v = kMax ? warp_max(v) : warp_sum(v);
+// Block-wide max / sum of one value per thread through `red` (32 slots); every thread gets the same result.
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
   const int warps = blockDim.x >> 5;
   float r = red[0];
-  for (int i = 1; i < warps; ++i) r = kMax ? fmaxf(r, red[i]) : r + red[i];
+  for (int i = 1; i < warps; ++i) r = fmaxf(r, red[i]);
+  return r;
+}
+__device__ __forceinline__ double block_sum(double v, double* red) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  const int warps = blockDim.x >> 5;
+  double r = red[0];
+  for (int i = 1; i < warps; ++i) r += red[i];
   return r;
 }
 
@@ -171,8 +196,11 @@ __global__ void __launch_bounds__(kClusterThreads) sm_cluster(const T* __restric
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t bars[kPieces];
   __shared__ float red[32];
-  __shared__ float part[2];  // this CTA's (max, sum), read by the peers
-  __shared__ float stat[2];  // the row's (max, sum)
+  __shared__ double red_d[32];
+  __shared__ float part_max;   // this CTA's max, read by the peers
+  __shared__ double part_sum;  // this CTA's sum, read by the peers
+  __shared__ float row_max;
+  __shared__ double row_sum;
 
   cg::cluster_group cluster = cg::this_cluster();
   const unsigned rank = cluster.block_rank();
@@ -221,43 +249,39 @@ __global__ void __launch_bounds__(kClusterThreads) sm_cluster(const T* __restric
     }
   }
   if (!ok) atomicOr(&g_softmax_status, CKB_STATUS_TIMEOUT);
-  m = block_fold<true>(m, red);
-  if (threadIdx.x == 0) part[0] = m;
+  m = block_max(m, red);
+  if (threadIdx.x == 0) part_max = m;
   cluster_arrive();
   cluster_wait();
   if (threadIdx.x < 32) {
-    float pm = threadIdx.x < csize ? cluster.map_shared_rank(part, threadIdx.x)[0] : -CUDART_INF_F;
+    float pm = threadIdx.x < csize ? *cluster.map_shared_rank(&part_max, threadIdx.x) : -CUDART_INF_F;
     pm = warp_max(pm);
-    if (threadIdx.x == 0) stat[0] = pm;
+    if (threadIdx.x == 0) row_max = pm;
   }
   __syncthreads();
-  m = stat[0];
+  m = row_max;
 
   // Pass 2: sum of exp(x - max); fp32 slices keep the exponentials in place for pass 3.
-  float s = 0.0f;
+  double s = 0.0;
   for (int i = threadIdx.x; i < nv; i += blockDim.x) {
     float f[V];
     unpack16(buf[i], f, x);
-#pragma unroll
-    for (int j = 0; j < V; ++j) {
-      f[j] = expf(f[j] - m);
-      s += f[j];
-    }
+    s += (double)exp_vec(f, m);
     if constexpr (V == 4) buf[i] = pack16(f, x);
   }
-  s = block_fold<false>(s, red + 0);  // red is free again: every thread read it before the cluster barrier above
-  if (threadIdx.x == 0) part[1] = s;
+  s = block_sum(s, red_d);
+  if (threadIdx.x == 0) part_sum = s;
   cluster_arrive();
   cluster_wait();
   if (threadIdx.x < 32) {
-    float ps = threadIdx.x < csize ? cluster.map_shared_rank(part, threadIdx.x)[1] : 0.0f;
+    double ps = threadIdx.x < csize ? *cluster.map_shared_rank(&part_sum, threadIdx.x) : 0.0;
     ps = warp_sum(ps);
-    if (threadIdx.x == 0) stat[1] = ps;
+    if (threadIdx.x == 0) row_sum = ps;
   }
-  // Peers may still read this CTA's `part` until they pass the next cluster barrier; arrive now, wait at the end.
+  // Peers may still read this CTA's part_sum until they pass the next cluster barrier; arrive now, wait at the end.
   cluster_arrive();
   __syncthreads();
-  const float inv = 1.0f / stat[1];
+  const float inv = (float)(1.0 / row_sum);
 
   // Pass 3: normalise from shared memory, stream to HBM.
   for (int i = threadIdx.x; i < nv; i += blockDim.x) {
@@ -268,7 +292,7 @@ __global__ void __launch_bounds__(kClusterThreads) sm_cluster(const T* __restric
       for (int j = 0; j < V; ++j) f[j] *= inv;
     } else {
 #pragma unroll
-      for (int j = 0; j < V; ++j) f[j] = expf(f[j] - m) * inv;
+      for (int j = 0; j < V; ++j) f[j] = exp_shifted(f[j], m) * inv;
     }
     store16(reinterpret_cast<T*>(reinterpret_cast<uint4*>(dst) + i), f);
   }
@@ -276,43 +300,22 @@ __global__ void __launch_bounds__(kClusterThreads) sm_cluster(const T* __restric
 }
 
 // ----------------------------------------------------------------------------------------------- stream path ----
-__device__ __forceinline__ void online_merge(float& m, float& s, float om, float os) {
-  const float M = fmaxf(m, om);
-  if (M == -CUDART_INF_F) return;  // both empty or both all -inf: keep (-inf, 0)
-  s = s * expf(m - M) + os * expf(om - M);
-  m = M;
-}
-
-// One block per row, any alignment: online (max, sum) over the row, block merge, then a second read to normalise.
+// One block per row, any alignment: a pass for the max, one for the sum (fp64 per thread), one to write; the second
+// and third reads of a row mostly hit L2.
 template <typename T>
 __global__ void __launch_bounds__(1024) sm_stream(const T* __restrict__ x, T* __restrict__ y, long long cols) {
-  __shared__ float rm[32], rs[32];
+  __shared__ float red[32];
+  __shared__ double red_d[32];
   const T* xr = x + (long long)blockIdx.x * cols;
   T* yr = y + (long long)blockIdx.x * cols;
-  float m = -CUDART_INF_F, s = 0.0f;
-  for (long long i = threadIdx.x; i < cols; i += blockDim.x) {
-    const float a = to_f32(xr[i]);
-    if (a > m) {
-      s *= expf(m - a);
-      m = a;
-    }
-    s += expf(a - m);
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
-    online_merge(m, s, om, os);
-  }
-  const int warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
-  if ((threadIdx.x & 31) == 0) {
-    rm[warp] = m;
-    rs[warp] = s;
-  }
-  __syncthreads();
-  m = rm[0];
-  s = rs[0];
-  for (int i = 1; i < warps; ++i) online_merge(m, s, rm[i], rs[i]);
-  const float inv = 1.0f / s;
-  for (long long i = threadIdx.x; i < cols; i += blockDim.x) yr[i] = from_f32<T>(expf(to_f32(xr[i]) - m) * inv);
+  float m = -CUDART_INF_F;
+  for (long long i = threadIdx.x; i < cols; i += blockDim.x) m = fmaxf(m, to_f32(xr[i]));
+  m = block_max(m, red);
+  double s = 0.0;
+  for (long long i = threadIdx.x; i < cols; i += blockDim.x) s += (double)exp_shifted(to_f32(xr[i]), m);
+  s = block_sum(s, red_d);
+  const float inv = (float)(1.0 / s);
+  for (long long i = threadIdx.x; i < cols; i += blockDim.x) yr[i] = from_f32<T>(exp_shifted(to_f32(xr[i]), m) * inv);
 }
 
 // ------------------------------------------------------------------------------------------------- dispatch -----

@@ -8,11 +8,13 @@
 //
 // Algorithm (one CTA per chunk of a row, 512 threads):
 //   1. the chunk is pulled into shared memory by bulk copies (cp.async.bulk, several pieces on their own mbarriers);
-//   2. radix select on the composites: a 4096-bin histogram of the top 12 bits (built as the pieces land), the bin
-//      holding the k-th largest is found by a block suffix scan; if the elements at or above that bin exceed the
-//      candidate buffer (2048), the next digit of the composites inside that bin is histogrammed, and so on
-//      (digits 12/10/10 over the key, 12/10/10 over the index, so ties on the value resolve by index);
-//   3. one pass collects the composites at or above the selected bin's lower edge (typically k + a few dozen);
+//   2. a lower bound: each thread keeps the max key of its elements (one pass as the pieces land); the k-th largest
+//      of those 512 maxima has at least k elements at or above it, so the lower edge of its bin in a 4096-bin
+//      histogram of the maxima' top 12 bits (found by a block suffix scan) bounds the chunk's k-th largest key;
+//   3. one pass collects the composites at or above that edge (typically k + a few dozen). If they overflow the
+//      2048-entry candidate buffer (heavy ties), a radix select over the composites narrows the edge first: the
+//      digit bin holding the k-th largest, refined digit by digit (12/10/10 bits of the key, 12/10/10 of the index,
+//      so ties on the value resolve by index) until the composites at or above it fit;
 //   4. a warp bitonic sort (up to 128 candidates, 4 per lane) or a block rank count leaves the chunk's top k sorted;
 //   5. a row split over several chunks writes each chunk's sorted top k to the workspace; the row's last CTA to finish
 //      (per-row counter, reset by that CTA) merges the sorted lists by rank (binary search of every candidate in the
@@ -142,6 +144,110 @@ __device__ __forceinline__ void warp_sort_desc(u64 (&v)[P]) {
   }
 }
 
+// The bin of a 2^w-bin histogram (w = 10 or 12) that holds the kk-th largest counted item, scanning from the top:
+// thread t owns bins [t * per, (t + 1) * per). Writes *s_bin and *s_above (the items in higher bins); *s_bin keeps
+// its previous value when fewer than kk items were counted. All threads call it; it ends with a barrier.
+__device__ __forceinline__ void find_bin(const unsigned* hist, int w, unsigned kk, unsigned* warp_tot, int* s_bin,
+                                         unsigned* s_above) {
+  const int per = (1 << w) / kThreads;
+  unsigned mine = 0;
+  for (int b = 0; b < per; ++b) mine += hist[threadIdx.x * per + b];
+  unsigned run = block_suffix_excl(mine, warp_tot);
+  for (int b = per - 1; b >= 0; --b) {
+    const unsigned h = hist[threadIdx.x * per + b];
+    if (run < kk && run + h >= kk) {
+      *s_bin = threadIdx.x * per + b;
+      *s_above = run;
+    }
+    run += h;
+  }
+  __syncthreads();
+}
+
+// Appends every staged composite >= lo to cand (warp-aggregated; at most kCap stored, *s_cnt counts them all).
+// A vector whose keys all lie below lo's key is skipped after one vote.
+template <typename T>
+__device__ __forceinline__ void collect(const uint4* data, int nv, int n, unsigned base_idx, u64 lo, u64* cand,
+                                        int* s_cnt) {
+  constexpr int V = VecN<T>::N;
+  const T* tag = nullptr;
+  const unsigned key_lo = (unsigned)(lo >> 32);
+  const int lane = threadIdx.x & 31;
+  for (int i0 = 0; i0 < nv; i0 += kThreads) {
+    const int i = i0 + threadIdx.x;
+    unsigned key[V];
+    bool maybe = false;
+    if (i < nv) {
+      keys16(data[i], key, tag);
+#pragma unroll
+      for (int e = 0; e < V; ++e) maybe |= key[e] >= key_lo && i * V + e < n;
+    }
+    if (!__any_sync(0xffffffffu, maybe)) continue;
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const int idx = i * V + e;
+      u64 c = 0;
+      bool take = false;
+      if (maybe && idx < n) {
+        c = composite(key[e], base_idx + (unsigned)idx);
+        take = c >= lo;
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, take);
+      if (m) {
+        int at = 0;
+        if (lane == 0) at = atomicAdd(s_cnt, __popc(m));
+        at = __shfl_sync(0xffffffffu, at, 0);
+        if (take) {
+          const int pos = at + __popc(m & ((1u << lane) - 1u));
+          if (pos < kCap) cand[pos] = c;
+        }
+      }
+    }
+  }
+}
+
+// Radix select over all staged composites: the lower edge `lo` of the digit bin holding the kk-th largest, refined
+// digit by digit (12/10/10 bits of the key, then 12/10/10 of the index) until the composites >= lo fit kCap. Every
+// level zeroes and rebuilds the histogram. All threads call it, after a barrier that ends all use of `hist`.
+template <typename T>
+__device__ u64 radix_select(const uint4* data, int nv, int n, unsigned base_idx, unsigned kk0, unsigned* hist,
+                            unsigned* warp_tot, int* s_bin, unsigned* s_above) {
+  constexpr int V = VecN<T>::N;
+  const T* tag = nullptr;
+  u64 prefix = 0, lo = 0;
+  unsigned kk = kk0, above_total = 0;
+  for (int L = 0; L < kLevels; ++L) {
+    const int sh = level_shift(L), w = level_width(L);
+    const unsigned mask = (1u << w) - 1u;
+    for (int i = threadIdx.x; i < kBins; i += kThreads) hist[i] = 0u;
+    __syncthreads();
+    for (int i = threadIdx.x; i < nv; i += kThreads) {
+      unsigned key[V];
+      keys16(data[i], key, tag);
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        const int idx = i * V + e;
+        if (idx < n) {
+          const u64 c = composite(key[e], base_idx + (unsigned)idx);
+          if (L == 0 || (c >> (sh + w)) == prefix) atomicAdd(&hist[(unsigned)(c >> sh) & mask], 1u);
+        }
+      }
+    }
+    __syncthreads();
+    find_bin(hist, w, kk, warp_tot, s_bin, s_above);
+    const int bin = *s_bin;
+    const unsigned above = *s_above, inbin = hist[bin];
+    const u64 next = (prefix << w) | (u64)bin;
+    lo = next << sh;
+    if (above_total + above + inbin <= (unsigned)kCap || L == kLevels - 1) break;
+    above_total += above;
+    kk -= above;
+    prefix = next;
+    __syncthreads();  // every thread has read hist[bin] and the bin before the next level rewrites them
+  }
+  return lo;
+}
+
 struct ChunkArgs {
   const void* x;
   void* values;          // mode 0: [rows, k] in x's dtype
@@ -213,108 +319,57 @@ __global__ void __launch_bounds__(kThreads) topk_chunk(const ChunkArgs a) {
   }
   for (int i = threadIdx.x; i < kBins; i += kThreads) hist[i] = 0u;
   if (threadIdx.x == 0) {
-    s_bin = 0;
+    s_bin = -1;
     s_above = 0u;
     s_cnt = 0;
   }
   __syncthreads();
 
-  // 2. Radix select: find the lower edge `lo` of the bin holding the k-th largest composite, refining until the
-  //    composites at or above it fit the candidate buffer.
-  const unsigned kk0 = (unsigned)min(a.k, n);
-  u64 lo = 0;
+  // 2. A lower bound from the per-thread maxima: the k-th largest of them has at least k elements at or above it, so
+  //    the lower edge of its histogram bin bounds the chunk's k-th largest key from below. Only 512 maxima touch the
+  //    histogram; the one pass over the chunk is a max.
   bool ok = true;
-  if (n <= kCap) {
-    if constexpr (kBulk) {
+  unsigned tmax = 0;
+  bool has = false;
+  for (int p = 0; p < kPieces; ++p) {
+    const int v0 = p * pv, v1 = min(nv, v0 + pv);
+    if (v1 <= v0) continue;
+    if constexpr (kBulk) ok = mbar_wait(&bars[p], 0) && ok;
+    for (int i = v0 + threadIdx.x; i < v1; i += kThreads) {
+      unsigned key[V];
+      keys16(data[i], key, tag);
 #pragma unroll
-      for (int p = 0; p < kPieces; ++p)
-        if (min(nv, p * pv + pv) > p * pv) ok = mbar_wait(&bars[p], 0) && ok;
-    }
-  } else {
-    u64 prefix = 0;
-    unsigned kk = kk0, above_total = 0;
-    for (int L = 0; L < kLevels; ++L) {
-      const int sh = level_shift(L), w = level_width(L);
-      const unsigned mask = (1u << w) - 1u;
-      for (int p = 0; p < kPieces; ++p) {
-        const int v0 = p * pv, v1 = min(nv, v0 + pv);
-        if (v1 <= v0) continue;
-        if constexpr (kBulk) {
-          if (L == 0) ok = mbar_wait(&bars[p], 0) && ok;
+      for (int e = 0; e < V; ++e)
+        if (i * V + e < n) {
+          tmax = key[e] > tmax ? key[e] : tmax;
+          has = true;
         }
-        for (int i = v0 + threadIdx.x; i < v1; i += kThreads) {
-          unsigned key[V];
-          keys16(data[i], key, tag);
-#pragma unroll
-          for (int e = 0; e < V; ++e) {
-            const int idx = i * V + e;
-            if (idx < n) {
-              const u64 c = composite(key[e], base_idx + (unsigned)idx);
-              if (L == 0 || (c >> (sh + w)) == prefix) atomicAdd(&hist[(unsigned)(c >> sh) & mask], 1u);
-            }
-          }
-        }
-      }
-      __syncthreads();
-      // Boundary bin: thread t owns bins [t * per, (t + 1) * per); scan from the top.
-      const int per = (1 << w) / kThreads;
-      unsigned mine = 0;
-      for (int b = 0; b < per; ++b) mine += hist[threadIdx.x * per + b];
-      unsigned run = block_suffix_excl(mine, warp_tot);
-      for (int b = per - 1; b >= 0; --b) {
-        const unsigned h = hist[threadIdx.x * per + b];
-        if (run < kk && run + h >= kk) {
-          s_bin = threadIdx.x * per + b;
-          s_above = run;
-        }
-        run += h;
-      }
-      __syncthreads();
-      const int bin = s_bin;
-      const unsigned above = s_above, inbin = hist[bin];
-      const u64 next = (prefix << w) | (u64)bin;
-      lo = next << sh;
-      if (above_total + above + inbin <= (unsigned)kCap || L == kLevels - 1) break;
-      above_total += above;
-      kk -= above;
-      prefix = next;
-      __syncthreads();  // every thread has read hist[bin]
-      for (int i = threadIdx.x; i < kBins; i += kThreads) hist[i] = 0u;
-      __syncthreads();
     }
   }
   if (!ok) atomicOr(&g_topk_status, CKB_STATUS_TIMEOUT);
+  const unsigned kk0 = (unsigned)min(a.k, n);
+  u64 lo = 0;
+  if (n > kCap) {
+    if (has) atomicAdd(&hist[tmax >> 20], 1u);
+    __syncthreads();
+    find_bin(hist, 12, kk0, warp_tot, &s_bin, &s_above);
+    if (s_bin >= 0) lo = (u64)s_bin << 52;
+  }
   __syncthreads();  // the histogram is dead from here: the candidate buffer reuses it
 
-  // 3. Collect the composites >= lo (warp-aggregated appends).
-  const int lane = threadIdx.x & 31;
-  for (int i0 = 0; i0 < nv; i0 += kThreads) {
-    const int i = i0 + threadIdx.x;
-    unsigned key[V];
-    if (i < nv) keys16(data[i], key, tag);
-#pragma unroll
-    for (int e = 0; e < V; ++e) {
-      const int idx = i * V + e;
-      u64 c = 0;
-      bool take = false;
-      if (i < nv && idx < n) {
-        c = composite(key[e], base_idx + (unsigned)idx);
-        take = c >= lo;
-      }
-      const unsigned m = __ballot_sync(0xffffffffu, take);
-      if (m) {
-        int at = 0;
-        if (lane == 0) at = atomicAdd(&s_cnt, __popc(m));
-        at = __shfl_sync(0xffffffffu, at, 0);
-        if (take) {
-          const int pos = at + __popc(m & ((1u << lane) - 1u));
-          if (pos < kCap) cand[pos] = c;
-        }
-      }
-    }
-  }
+  // 3. Collect the composites >= lo. If they overflow the buffer (heavy ties, or too few maxima), a full radix select
+  //    over the chunk's composites narrows `lo` until they fit, and they are collected again.
+  collect<T>(data, nv, n, base_idx, lo, cand, &s_cnt);
   __syncthreads();
+  if (s_cnt > kCap) {
+    lo = radix_select<T>(data, nv, n, base_idx, kk0, hist, warp_tot, &s_bin, &s_above);
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    collect<T>(data, nv, n, base_idx, lo, cand, &s_cnt);
+    __syncthreads();
+  }
   const int cnt = min(s_cnt, kCap);
+  const int lane = threadIdx.x & 31;
 
   // 4. The chunk's top k, sorted, into top[0, k) (zero padded when the chunk has fewer than k elements).
   if (cnt <= kSortMax) {

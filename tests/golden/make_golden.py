@@ -124,7 +124,7 @@ def make_rope(out):
 
 
 def make_topk(out):
-    # plan + launch as topk/candidate.py:71,90-91 call them (K 50, threads 256, depth 4, min_chunk 2048).
+    # plan + launch as topk/candidate.py:58,77-78 call them (K 50, threads 256, depth 4, min_chunk 2048).
     lib = _ref("topk")
     lib.plan.argtypes = [ctypes.c_longlong, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
     lib.plan.restype = ctypes.c_longlong
