@@ -446,6 +446,9 @@ def main():
 
     from ckb200 import workloads
 
+    if args.workload == "topk_vocab_512x151936":
+        run_vocab(args, rank, world, local)
+        return
     peak, peak_kind = hbm_peak()
     case = make_case(args.workload)
     ms, clocks = time_case(case, args.steps, args.warmup, world, sampler_gpu=local)
@@ -476,6 +479,52 @@ def main():
     if world == 1 and rank == 0 and not args.no_sweep:
         line["kernels"] = sweep(args, world)
     if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_vocab(args, rank, world, local):
+    """Vocab-sharded top-k (strong scaling): the [512, 151936] fp32 logits split by columns over the ranks; a step is
+    the local top-50 kernel, one NCCL all-gather of the [512, 50] composite lists and the merge kernel."""
+    from ckb200 import sharded, workloads
+
+    peak, peak_kind = hbm_peak()
+    dev = torch.device("cuda", local)
+    full = workloads.topk_512x151936()["x"]
+    lo, hi = sharded.col_range(full.shape[1], rank, world)
+    shards = [full[:, lo:hi].contiguous().to(dev) for _ in range(2)]  # two copies: rotate past L2
+    op = sharded.VocabShardedTopK(full.shape[0], 50, device=dev)
+    for i in range(args.warmup):
+        op(shards[i % 2], lo)
+    torch.cuda.synchronize()
+    barrier(world)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    sampler.__enter__()
+    start.record()
+    for i in range(args.steps):
+        values, indices = op(shards[i % 2], lo)
+    end.record()
+    torch.cuda.synchronize()
+    sampler.__exit__(None, None, None)
+    ms = max_over_ranks(start.elapsed_time(end), world)
+    nbytes = workloads.ALGORITHMIC_BYTES["topk_512x151936"]
+    ok = None
+    if rank == 0:
+        from oracle import topk as otk
+        wv, wi = otk.topk(full, 50)
+        ok = bool(torch.equal(indices.cpu(), wi) and torch.equal(values.cpu(), wv))
+        line = {"metric": METRIC, "value": round(nbytes * args.steps / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded, BASELINE config distributions)",
+                "config": {"workload": args.workload, "cols_per_gpu": hi - lo, "parallelism": f"vocab-sharded x{world}",
+                           "collective": "NCCL all_gather_into_tensor of [512, 50] int64 composites"},
+                "rows_per_s": round(512 * args.steps / (ms * 1e-3), 1),
+                "roofline": {"bound": "hbm", "achieved": round(nbytes / world / (ms / args.steps * 1e-3) / 1e9, 1),
+                             "peak": peak, "unit": "GB/s per GPU", "peak_kind": peak_kind},
+                "clocks": sampler.summary(), "gpu_launches": 2 * args.steps, "check": ok}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -46,3 +46,27 @@ def topk_vocab_sharded(x_shard, col_offset, k=_topk.K, group=None):
     columns [col_offset, col_offset + local_cols). Every rank returns the same (values, indices) [rows, k]."""
     lists = _topk.shard_lists(x_shard, col_offset, k)
     return _topk.merge_lists(gather_lists(lists, group), x_shard.dtype, k)
+
+
+class VocabShardedTopK:
+    """topk_vocab_sharded with every buffer allocated once (for repeated calls on one shape): the local lists, the
+    gathered [world, rows, k] lists and the outputs. A call launches the shard kernel, one NCCL all-gather and the
+    merge kernel on the current stream."""
+
+    def __init__(self, rows, k=_topk.K, dtype=None, device=None, group=None):
+        self.group = group
+        self.k = k
+        self.dtype = dtype
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.lists = torch.empty((rows, k), dtype=torch.int64, device=device)
+        self.gathered = torch.empty((self.world, rows, k), dtype=torch.int64, device=device)
+
+    def __call__(self, x_shard, col_offset):
+        _topk.shard_lists(x_shard, col_offset, self.k, out=self.lists)
+        if self.world == 1:
+            self.gathered[0].copy_(self.lists)
+        elif dist.get_backend(self.group) == "nccl":
+            dist.all_gather_into_tensor(self.gathered, self.lists, group=self.group)
+        else:
+            dist.all_gather(list(self.gathered.unbind(0)), self.lists, group=self.group)
+        return _topk.merge_lists(self.gathered, x_shard.dtype, self.k)

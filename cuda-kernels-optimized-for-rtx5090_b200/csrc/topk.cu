@@ -8,10 +8,12 @@
 //
 // Algorithm (one CTA per chunk of a row, 512 threads):
 //   1. the chunk is pulled into shared memory by bulk copies (cp.async.bulk, several pieces on their own mbarriers);
-//   2. a lower bound: each thread keeps the max key of its elements (one pass as the pieces land); the k-th largest
-//      of those 512 maxima has at least k elements at or above it, so the lower edge of its bin in a 4096-bin
-//      histogram of the maxima' top 12 bits (found by a block suffix scan) bounds the chunk's k-th largest key;
-//   3. one pass collects the composites at or above that edge (typically k + a few dozen). If they overflow the
+//   2. a lower bound: each thread keeps the max of its numbers (one fmax per element as the pieces land); the k-th
+//      largest of those 512 maxima has at least k elements at or above it, so the lower edge of its bin in a
+//      4096-bin histogram of the maxima's top 12 key bits (found by a block suffix scan) bounds the chunk's k-th
+//      largest key from below;
+//   3. one pass collects the composites at or above that edge (typically k + a few dozen): a float compare per
+//      element, and the composite only for the few that pass. If they overflow the
 //      2048-entry candidate buffer (heavy ties), a radix select over the composites narrows the edge first: the
 //      digit bin holding the k-th largest, refined digit by digit (12/10/10 bits of the key, 12/10/10 of the index,
 //      so ties on the value resolve by index) until the composites at or above it fit;
@@ -41,7 +43,10 @@ constexpr int kCap = 2048;             // candidate buffer (aliases the histogra
 constexpr int kMaxK = 512;
 constexpr int kPieces = 4;
 constexpr int kLevels = 6;
-constexpr int kChunkBytes = 48 * 1024;  // staged bytes per CTA: chunk + histogram keep 3 CTAs per SM
+#ifndef CKB_TOPK_CHUNK_BYTES
+#define CKB_TOPK_CHUNK_BYTES (48 * 1024)
+#endif
+constexpr int kChunkBytes = CKB_TOPK_CHUNK_BYTES;  // staged bytes per CTA: chunk + histogram keep 3 CTAs per SM
 constexpr int kMaxDataBytes = 160 * 1024;
 constexpr int kSortMax = 128;          // warp bitonic sort: 4 composites per lane
 
@@ -69,6 +74,48 @@ __device__ __forceinline__ void keys16(const uint4& r, unsigned (&k)[8], const _
     k[2 * j] = order_key(w[j] << 16);
     k[2 * j + 1] = order_key(w[j] & 0xffff0000u);
   }
+}
+
+// The largest non-NaN value of one staged 16-byte vector folded into a running max (NaN inputs are skipped, so a
+// running max that is still NaN has seen no number).
+__device__ __forceinline__ float vec_max(const uint4& r, float m, const float*) {
+  m = fmaxf(m, __uint_as_float(r.x));
+  m = fmaxf(m, __uint_as_float(r.y));
+  m = fmaxf(m, __uint_as_float(r.z));
+  return fmaxf(m, __uint_as_float(r.w));
+}
+__device__ __forceinline__ float vec_max(const uint4& r, float m, const __nv_bfloat16*) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
+  const __nv_bfloat162 a = __hmax2(h[0], h[1]), b = __hmax2(h[2], h[3]);
+  const __nv_bfloat162 c = __hmax2(a, b);
+  return fmaxf(m, fmaxf(__low2float(c), __high2float(c)));
+}
+
+// The fp32 bits of element e of one staged vector (a bf16 element widened).
+__device__ __forceinline__ unsigned word_of(const uint4& r, int j) {
+  return j < 2 ? (j == 0 ? r.x : r.y) : (j == 2 ? r.z : r.w);
+}
+__device__ __forceinline__ unsigned elem_bits(const uint4& r, int e, const float*) { return word_of(r, e); }
+__device__ __forceinline__ unsigned elem_bits(const uint4& r, int e, const __nv_bfloat16*) {
+  const unsigned w = word_of(r, e >> 1);
+  return (e & 1) ? (w & 0xffff0000u) : (w << 16);
+}
+
+// Bit mask (bit e) of the elements of one staged vector that are not below f_lo as floats, NaN included: a superset
+// of the elements whose order key is >= the key of f_lo.
+__device__ __forceinline__ unsigned vec_not_below(const uint4& r, float f_lo, const float*) {
+  return (unsigned)!(__uint_as_float(r.x) < f_lo) | ((unsigned)!(__uint_as_float(r.y) < f_lo) << 1) |
+         ((unsigned)!(__uint_as_float(r.z) < f_lo) << 2) | ((unsigned)!(__uint_as_float(r.w) < f_lo) << 3);
+}
+__device__ __forceinline__ unsigned vec_not_below(const uint4& r, float f_lo, const __nv_bfloat16*) {
+  const unsigned w[4] = {r.x, r.y, r.z, r.w};
+  unsigned m = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    m |= (unsigned)!(__uint_as_float(w[j] << 16) < f_lo) << (2 * j);
+    m |= (unsigned)!(__uint_as_float(w[j] & 0xffff0000u) < f_lo) << (2 * j + 1);
+  }
+  return m;
 }
 
 template <typename T>
@@ -164,43 +211,26 @@ __device__ __forceinline__ void find_bin(const unsigned* hist, int w, unsigned k
   __syncthreads();
 }
 
-// Appends every staged composite >= lo to cand (warp-aggregated; at most kCap stored, *s_cnt counts them all).
-// A vector whose keys all lie below lo's key is skipped after one vote.
+// Appends every staged composite >= lo to cand (at most kCap stored, *s_cnt counts them all). A float compare finds
+// the few elements that may qualify; only those build their composite and take a slot with a shared atomic.
 template <typename T>
 __device__ __forceinline__ void collect(const uint4* data, int nv, int n, unsigned base_idx, u64 lo, u64* cand,
                                         int* s_cnt) {
   constexpr int V = VecN<T>::N;
   const T* tag = nullptr;
-  const unsigned key_lo = (unsigned)(lo >> 32);
-  const int lane = threadIdx.x & 31;
-  for (int i0 = 0; i0 < nv; i0 += kThreads) {
-    const int i = i0 + threadIdx.x;
-    unsigned key[V];
-    bool maybe = false;
-    if (i < nv) {
-      keys16(data[i], key, tag);
-#pragma unroll
-      for (int e = 0; e < V; ++e) maybe |= key[e] >= key_lo && i * V + e < n;
-    }
-    if (!__any_sync(0xffffffffu, maybe)) continue;
-#pragma unroll
-    for (int e = 0; e < V; ++e) {
+  const float f_lo = __uint_as_float(key_bits((unsigned)(lo >> 32)));
+  for (int i = threadIdx.x; i < nv; i += kThreads) {
+    const uint4 r = data[i];
+    unsigned mask = vec_not_below(r, f_lo, tag);
+    if (mask == 0u) continue;
+    while (mask) {
+      const int e = __ffs(mask) - 1;
+      mask &= mask - 1u;
       const int idx = i * V + e;
-      u64 c = 0;
-      bool take = false;
-      if (maybe && idx < n) {
-        c = composite(key[e], base_idx + (unsigned)idx);
-        take = c >= lo;
-      }
-      const unsigned m = __ballot_sync(0xffffffffu, take);
-      if (m) {
-        int at = 0;
-        if (lane == 0) at = atomicAdd(s_cnt, __popc(m));
-        at = __shfl_sync(0xffffffffu, at, 0);
-        if (take) {
-          const int pos = at + __popc(m & ((1u << lane) - 1u));
-          if (pos < kCap) cand[pos] = c;
-        }
+      const u64 c = composite(order_key(elem_bits(r, e, tag)), base_idx + (unsigned)idx);
+      if (idx < n && c >= lo) {
+        const int pos = atomicAdd(s_cnt, 1);
+        if (pos < kCap) cand[pos] = c;
       }
     }
   }
@@ -316,8 +346,10 @@ __global__ void __launch_bounds__(kThreads) topk_chunk(const ChunkArgs a) {
   } else {
     T* d = reinterpret_cast<T*>(data);
     for (int i = threadIdx.x; i < n; i += kThreads) d[i] = src[i];
+    // Pad the last vector with NaN: the max pass skips it and the collect pass rejects it by index.
+    for (int i = n + threadIdx.x; i < nv * V; i += kThreads) d[i] = from_f32<T>(__int_as_float(0x7fc00000));
   }
-  for (int i = threadIdx.x; i < kBins; i += kThreads) hist[i] = 0u;
+  for (int i = threadIdx.x; i < kBins / 4; i += kThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0u, 0u, 0u, 0u);
   if (threadIdx.x == 0) {
     s_bin = -1;
     s_above = 0u;
@@ -329,28 +361,19 @@ __global__ void __launch_bounds__(kThreads) topk_chunk(const ChunkArgs a) {
   //    the lower edge of its histogram bin bounds the chunk's k-th largest key from below. Only 512 maxima touch the
   //    histogram; the one pass over the chunk is a max.
   bool ok = true;
-  unsigned tmax = 0;
-  bool has = false;
+  float fmax = __int_as_float(0x7fc00000);  // NaN: no number seen yet
   for (int p = 0; p < kPieces; ++p) {
     const int v0 = p * pv, v1 = min(nv, v0 + pv);
     if (v1 <= v0) continue;
     if constexpr (kBulk) ok = mbar_wait(&bars[p], 0) && ok;
-    for (int i = v0 + threadIdx.x; i < v1; i += kThreads) {
-      unsigned key[V];
-      keys16(data[i], key, tag);
-#pragma unroll
-      for (int e = 0; e < V; ++e)
-        if (i * V + e < n) {
-          tmax = key[e] > tmax ? key[e] : tmax;
-          has = true;
-        }
-    }
+    for (int i = v0 + threadIdx.x; i < v1; i += kThreads) fmax = vec_max(data[i], fmax, tag);
   }
   if (!ok) atomicOr(&g_topk_status, CKB_STATUS_TIMEOUT);
   const unsigned kk0 = (unsigned)min(a.k, n);
   u64 lo = 0;
   if (n > kCap) {
-    if (has) atomicAdd(&hist[tmax >> 20], 1u);
+    // fmax is one of this thread's elements (or NaN when it has no number): the maxima counted are real elements.
+    if (fmax == fmax) atomicAdd(&hist[order_key(__float_as_uint(fmax)) >> 20], 1u);
     __syncthreads();
     find_bin(hist, 12, kk0, warp_tot, &s_bin, &s_above);
     if (s_bin >= 0) lo = (u64)s_bin << 52;
