@@ -33,6 +33,7 @@ SIGNATURES = {
         "launch": (_INT, [_VP] * 5 + [_LL, _LL, _INT, _INT, _INT, _INT, _LL, _VP]),
         "ckb_topk_shard_launch": (_INT, [_VP] * 4 + [_LL, _LL, _LL, _INT, _INT, _LL, _VP]),
         "ckb_topk_merge_launch": (_INT, [_VP, _INT, _VP, _VP, _LL, _INT, _INT, _VP]),
+        "ckb_topk_launch_noalloc": (_INT, [_VP, _VP, _VP, _LL, _LL, _INT, _INT, _VP]),
         "ckb_topk_status": (_INT, [_INT]),
     },
 }

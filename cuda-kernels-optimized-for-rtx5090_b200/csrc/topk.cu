@@ -627,3 +627,71 @@ CKB_EXPORT int ckb_topk_status(int reset) {
   }
   return (int)v;
 }
+
+// ------------------------------------------------------------------------------------------ no-allocation entry ---
+// Some callers cannot allocate device memory for the workspace and counters that launch() takes: code living inside
+// a host framework that hands out a fixed budget through its own allocator (and may have reserved nearly all of the
+// GPU up front), or a latency-critical path where cudaMalloc's implicit device synchronisation is not acceptable.
+// ckb_topk_launch_noalloc serves them from a scratch array compiled into this library instead: 4 MiB of device
+// memory that every GPU which loads the library holds until the process exits. The first 256 KiB are the per-row
+// counters (up to 65536 rows), the rest the chunk workspace (491,520 composites, i.e. rows * chunks * k at most that).
+constexpr size_t kNoAllocBytes = size_t(4) << 20;
+static __device__ __align__(256) unsigned long long g_noalloc_scratch[kNoAllocBytes / 8];
+
+namespace ckb {
+namespace {
+
+constexpr long long kNoAllocCounterWords = 32768;  // 65536 uint32 counters in the first 256 KiB
+constexpr long long kNoAllocWorkWords = (long long)(kNoAllocBytes / 8) - kNoAllocCounterWords;
+
+// The scratch array's device address on the current device. In host code g_noalloc_scratch names a host-side
+// stand-in, not device memory, so the address is looked up once per device (with that device current) and cached.
+cudaError_t noalloc_scratch(void** out) {
+  static std::atomic<void*> cache[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  void* p = cache[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    cache[dev].store(p, std::memory_order_release);
+  }
+  *out = p;
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace ckb
+
+// The top-k of launch() without any caller-provided workspace or counters (no counterpart in the reference): values
+// [rows, k] in x's dtype and int64 indices [rows, k] of x [rows, cols], dtype 0 (fp32) or 1 (bf16), planned as plan()
+// would with min_chunk 2048. Allocates nothing. Returns 0, -1 for arguments launch() would also reject, -2 when the
+// plan needs more than the static scratch holds (rows * chunks * k > 491,520 or rows > 65,536), or a cudaError_t.
+// The first call on a device looks up the scratch address (make it before any stream capture). Every call shares the
+// one scratch array, so calls that overlap on the GPU (different streams, no ordering between them) race; calls on
+// one stream are ordered. The counters are cleared on the caller's stream at each call.
+CKB_EXPORT int ckb_topk_launch_noalloc(const void* x, void* values, void* indices, long long rows, long long cols,
+                                       int k, int dtype, cudaStream_t stream) {
+  if (rows <= 0 || k <= 0) return 0;
+  if (dtype != kF32 && dtype != kBF16) return -1;
+  const int elem = dtype == kBF16 ? 2 : 4;
+  long long chunk = plan_chunk(rows, cols, elem, 2048);
+  if (bad_args(rows, cols, k, chunk, elem)) return -1;
+  if (chunk > cols) chunk = cols;
+  const long long nchunks = (cols + chunk - 1) / chunk;
+  if (rows > 2 * kNoAllocCounterWords || (nchunks > 1 && rows * nchunks * k > kNoAllocWorkWords)) return -2;
+  void* base = nullptr;
+  cudaError_t e = noalloc_scratch(&base);
+  if (e != cudaSuccess) return (int)e;
+  unsigned* counters = reinterpret_cast<unsigned*>(base);
+  u64* work = reinterpret_cast<u64*>(base) + kNoAllocCounterWords;
+  if (nchunks > 1) {
+    e = cudaMemsetAsync(counters, 0, (size_t)rows * sizeof(unsigned), stream);
+    if (e != cudaSuccess) return (int)e;
+  }
+  ChunkArgs a{x, values, (long long*)indices, nullptr, work, counters, 0, 0, 0, k, 0, 0};
+  if (dtype == kF32) return start_chunk<float>(a, rows, cols, chunk, stream);
+  return start_chunk<__nv_bfloat16>(a, rows, cols, chunk, stream);
+}

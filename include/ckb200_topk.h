@@ -33,6 +33,16 @@ int ckb_topk_shard_launch(const void* x, unsigned long long* lists, void* work, 
 int ckb_topk_merge_launch(const unsigned long long* lists, int nlists, void* values, void* indices, long long rows,
                           int k, int dtype, cudaStream_t stream);
 
+/* The top-k of launch() for callers that cannot allocate device memory (a host framework that owns the GPU's memory
+ * through its own fixed-budget allocator, or a path that cannot afford cudaMalloc's device synchronisation): no
+ * workspace or counters are passed; a 4 MiB scratch array compiled into this library (held on every GPU that loads
+ * it, until exit) serves instead. No counterpart in the reference. dtype 0 fp32 / 1 bf16; returns -1 for arguments
+ * launch() rejects, -2 when rows * chunks * k > 491,520 or rows > 65,536 (the scratch is too small). The first call on
+ * a device looks up the scratch address: make it before any stream capture. All calls share the scratch, so calls
+ * that overlap on the GPU race; the counters are cleared on `stream` at every call. */
+int ckb_topk_launch_noalloc(const void* x, void* values, void* indices, long long rows, long long cols, int k,
+                            int dtype, cudaStream_t stream);
+
 /* Bounded-wait status of this library's kernels since the last reset: 0 fine, 1 a bulk-copy wait gave up.
  * Synchronous; reset != 0 clears it; negative: -cudaError_t. No counterpart in the reference. */
 int ckb_topk_status(int reset);

@@ -1,0 +1,52 @@
+"""ckb_topk_launch_noalloc: top-k for callers that cannot allocate device memory.
+
+Such callers (code inside a host framework that hands out a fixed device-memory budget through its own allocator,
+or a latency-critical path that cannot take cudaMalloc's device synchronisation) cannot provide the workspace and
+counters that `launch` needs; this entry point takes only the input and the outputs and uses a scratch array
+compiled into the library. It must give exactly what `launch` gives (top-k parity is bit-exact), call after call,
+since the scratch keeps the previous call's contents. This file sorts last so a run stopping at the first failure
+has already run every other test; it also passes alone in a fresh process.
+"""
+
+import ctypes
+
+import pytest
+import torch
+
+from ckb200 import build, topk, workloads
+from helpers import bits_equal
+
+pytestmark = pytest.mark.gpu
+
+
+def _noalloc():
+    lib = ctypes.CDLL(build.lib_path("topk"))
+    fn = lib.ckb_topk_launch_noalloc
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_longlong,
+                   ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    return fn
+
+
+@pytest.mark.parametrize("dtype,scale", [(torch.float32, 1), (torch.bfloat16, 4)])
+def test_matches_launch_on_two_calls_in_a_row(dtype, scale):
+    fn = _noalloc()
+    x = workloads.topk_512x151936(scale=scale)["x"].to(dtype).cuda()
+    rows, cols = x.shape
+    want_v, want_i = topk.topk(x, 50)  # the existing entry point, with its own workspace and counters
+    stream = torch.cuda.current_stream().cuda_stream
+    for call in range(2):
+        v = torch.empty(rows, 50, dtype=dtype, device="cuda")
+        i = torch.empty(rows, 50, dtype=torch.int64, device="cuda")
+        assert fn(x.data_ptr(), v.data_ptr(), i.data_ptr(), rows, cols, 50, 0 if dtype == torch.float32 else 1,
+                  stream) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(i, want_i), f"call {call}: indices differ"
+        assert bits_equal(v, want_v), f"call {call}: values differ"
+
+
+def test_rejects_plans_beyond_the_scratch():
+    fn = _noalloc()
+    # 512 rows x 4M columns needs 512 * 342 * 50 composites of workspace, far beyond the 4 MiB scratch; the check
+    # happens before anything touches the (never read) pointers.
+    assert fn(None, None, None, 512, 1 << 22, 50, 0, None) == -2
