@@ -361,7 +361,7 @@ def e2e_rmsnorm(steps, warmup, world):
 
 
 # --------------------------------------------------------------------------------------------- CPU baselines ----
-def cpu_sample_rate(name, min_seconds=10.0, max_reps=200, reps_exact=None):
+def cpu_sample_rate(name, min_seconds=10.0, max_reps=5000, reps_exact=None):
     """GB/s of the reference's CPU path (the oracle's torch restatement, all host threads) on a bounded sample of
     workload `name`: at least 3 repetitions and min_seconds (at most max_reps), or exactly reps_exact;
     returns (GB/s, sample description, threads)."""

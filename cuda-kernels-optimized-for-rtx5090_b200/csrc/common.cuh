@@ -149,16 +149,39 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
   return ok != 0u;
 }
 
+// try_wait that lets the hardware suspend the thread for up to kSuspendNs until the phase completes, so waiting
+// warps sleep instead of spinning through the issue slots.
+constexpr unsigned kSuspendNs = 100000u;
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0u;
+}
+
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any copy this library issues
 
-// Waits for the phase with the given parity to complete; false when the wait ran out of time.
+// Waits for the phase with the given parity to complete; false when the wait ran out of time. The clock is read only
+// every 64 tries.
+#ifndef CKB_MBAR_SUSPEND
+#define CKB_MBAR_SUSPEND 1
+#endif
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, unsigned parity) {
+  return CKB_MBAR_SUSPEND ? mbar_try_wait_suspend(bar, parity) : mbar_try_wait(bar, parity);
+}
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_poll(bar, parity)) return true;
   const unsigned long long start = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_poll(bar, parity)) return true;
     if (global_ns() - start > kWaitLimitNs) return false;
   }
-  return true;
 }
 
 // One bulk copy global -> this CTA's shared memory, completing `bytes` of transaction on `bar`. Addresses 16-byte
@@ -170,6 +193,9 @@ __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, unsig
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+
+// Orders this thread's generic-proxy shared-memory accesses before later bulk copies into the same bytes.
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Status word a kernel sets when a bounded wait gave up (0 = fine). One per library, read by <op>_status().
 #define CKB_STATUS_TIMEOUT 1u

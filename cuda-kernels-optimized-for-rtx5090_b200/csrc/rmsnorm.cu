@@ -170,7 +170,11 @@ __global__ void __launch_bounds__(1024) rms_generic(const T* __restrict__ x, con
 
 constexpr int kWarpRowsMaxVec = 128;      // warp path: at most 4 vectors per lane
 constexpr int kBlockRowsMaxVec = 4096;    // block path: at most 512 threads x 8 vectors
-constexpr int kBlockTargetThreads = 128;  // block path: VPT grows until a row needs at most this many threads
+#ifndef CKB_RMSNORM_TARGET_THREADS
+#define CKB_RMSNORM_TARGET_THREADS 128
+#endif
+constexpr int kBlockTargetThreads = CKB_RMSNORM_TARGET_THREADS;  // block path: VPT grows until a row needs at most
+                                                                 // this many threads
 
 template <typename T, typename WT, int VPT>
 void start_warp(const void* x, const void* w, void* y, long long rows, int cols, float eps, cudaStream_t s) {

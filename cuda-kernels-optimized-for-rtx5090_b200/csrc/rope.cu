@@ -10,7 +10,7 @@
 //
 // B200 mapping (HBM bound: q and k are streamed once; cos/sin rows are L2/L1 hits): thread (c, r, z) of a block owns
 // the 8 pairs 8c..8c+7 of head_dim in heads r, r + R, r + 2R, ... of token blockIdx.x * Z + z, so the cos/sin of its
-// pairs are loaded (or computed) once and reused over its heads; up to 4 heads (8 16-byte loads) are in flight per
+// pairs are loaded (or computed) once and reused over its heads; up to 5 heads (10 16-byte loads) are in flight per
 // thread. head_dim % 16 != 0 or an unaligned pointer falls back to a scalar kernel (one pair per thread).
 #include "ckb200_rope.h"
 #include "common.cuh"
@@ -20,7 +20,13 @@
 namespace ckb {
 namespace {
 
-constexpr int kHeadsInFlight = 4;
+#ifndef CKB_ROPE_HEADS_IN_FLIGHT
+#define CKB_ROPE_HEADS_IN_FLIGHT 5
+#endif
+#ifndef CKB_ROPE_MIN_BLOCKS
+#define CKB_ROPE_MIN_BLOCKS 1
+#endif
+constexpr int kHeadsInFlight = CKB_ROPE_HEADS_IN_FLIGHT;  // heads whose q/k loads one thread keeps in flight
 
 // 8 consecutive cache values as fp32 (i a multiple of 8; the row start 16-byte aligned).
 __device__ __forceinline__ void ld8(const float* p, long long i, float (&v)[8]) {
@@ -48,7 +54,7 @@ __device__ __forceinline__ uint4 ld_x(const void* p) {
 
 // kCache: cos/sin from the cache (C its dtype); otherwise sincosf(pos * inv_freq[i]).
 template <typename T, typename C, bool kCache, bool kInPlace>
-__global__ void __launch_bounds__(256) rope_vec(const T* q, const T* k, const C* __restrict__ cos_rows,
+__global__ void __launch_bounds__(256, CKB_ROPE_MIN_BLOCKS) rope_vec(const T* q, const T* k, const C* __restrict__ cos_rows,
                                                 const C* __restrict__ sin_rows, const float* __restrict__ inv_freq,
                                                 const long long* __restrict__ ids, T* q_out, T* k_out,
                                                 long long tokens, int q_heads, int kv_heads, int head_dim) {

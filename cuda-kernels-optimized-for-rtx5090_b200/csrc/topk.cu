@@ -9,15 +9,16 @@
 // Algorithm (one CTA per chunk of a row, 512 threads):
 //   1. the chunk is pulled into shared memory by bulk copies (cp.async.bulk, several pieces on their own mbarriers);
 //   2. a lower bound: each thread keeps the max of its numbers (one fmax per element as the pieces land); the k-th
-//      largest of those 512 maxima has at least k elements at or above it, so the lower edge of its bin in a
-//      4096-bin histogram of the maxima's top 12 key bits (found by a block suffix scan) bounds the chunk's k-th
-//      largest key from below;
+//      largest of those maxima has at least k elements at or above it, so the lower edge of its bin in a 2048-bin
+//      histogram of the maxima's top 11 key bits (found by a block suffix scan) bounds the chunk's k-th largest key
+//      from below;
 //   3. one pass collects the composites at or above that edge (typically k + a few dozen): a float compare per
-//      element, and the composite only for the few that pass. If they overflow the
-//      2048-entry candidate buffer (heavy ties), a radix select over the composites narrows the edge first: the
-//      digit bin holding the k-th largest, refined digit by digit (12/10/10 bits of the key, 12/10/10 of the index,
-//      so ties on the value resolve by index) until the composites at or above it fit;
-//   4. a warp bitonic sort (up to 128 candidates, 4 per lane) or a block rank count leaves the chunk's top k sorted;
+//      element, and the composite only for the few that pass, appended by each warp into its own slots of the
+//      candidate buffer (a warp prefix sum places them; no shared atomics). If a warp's slots overflow (heavy ties),
+//      a radix select over the composites narrows the edge first: the digit bin holding the k-th largest, refined
+//      digit by digit (11/11/10 bits of the key, 11/11/10 of the index, so value ties resolve by index) until the
+//      composites at or above it fit the 1024-entry buffer;
+//   4. a block rank count (several lanes per candidate) leaves the chunk's top k sorted;
 //   5. a row split over several chunks writes each chunk's sorted top k to the workspace; the row's last CTA to finish
 //      (per-row counter, reset by that CTA) merges the sorted lists by rank (binary search of every candidate in the
 //      other lists) and decodes values and indices from the composites (x is not read again).
@@ -25,6 +26,8 @@
 // composites; after an all-gather across GPUs the merge kernel ranks the per-GPU lists the same way.
 #include "ckb200_topk.h"
 #include "common.cuh"
+
+#include <math_constants.h>
 
 #include <climits>
 
@@ -36,24 +39,28 @@ namespace {
 
 typedef unsigned long long u64;
 
-constexpr int kThreads = 512;
+#ifndef CKB_TOPK_THREADS
+#define CKB_TOPK_THREADS 512
+#endif
+constexpr int kThreads = CKB_TOPK_THREADS;
 constexpr int kWarps = kThreads / 32;
-constexpr int kBins = 4096;            // largest digit: 12 bits
-constexpr int kCap = 2048;             // candidate buffer (aliases the histogram)
+constexpr int kBins = 2048;            // largest digit: 11 bits
+constexpr int kCap = 1024;             // candidate buffer (aliases the histogram)
+constexpr int kWarpSlots = kCap / kWarps;  // each warp appends into its own slice of the candidate buffer
 constexpr int kMaxK = 512;
 constexpr int kPieces = 4;
 constexpr int kLevels = 6;
 #ifndef CKB_TOPK_CHUNK_BYTES
-#define CKB_TOPK_CHUNK_BYTES (48 * 1024)
+#define CKB_TOPK_CHUNK_BYTES (96 * 1024)
 #endif
-constexpr int kChunkBytes = CKB_TOPK_CHUNK_BYTES;  // staged bytes per CTA: chunk + histogram keep 3 CTAs per SM
+constexpr int kChunkBytes = CKB_TOPK_CHUNK_BYTES;  // staged bytes per CTA: chunk + histogram keep 2 CTAs per SM
 constexpr int kMaxDataBytes = 160 * 1024;
-constexpr int kSortMax = 128;          // warp bitonic sort: 4 composites per lane
 
+// Radix digits over the 64-bit composite, most significant first: 11/11/10 bits of the key, then 11/11/10 of ~index.
 __device__ __forceinline__ int level_shift(int L) {
-  return L == 0 ? 52 : L == 1 ? 42 : L == 2 ? 32 : L == 3 ? 20 : L == 4 ? 10 : 0;
+  return L == 0 ? 53 : L == 1 ? 42 : L == 2 ? 32 : L == 3 ? 21 : L == 4 ? 10 : 0;
 }
-__device__ __forceinline__ int level_width(int L) { return (L == 0 || L == 3) ? 12 : 10; }
+__device__ __forceinline__ int level_width(int L) { return (L == 2 || L == 5) ? 10 : 11; }
 
 __device__ __forceinline__ unsigned order_key(unsigned bits) {
   return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
@@ -78,17 +85,45 @@ __device__ __forceinline__ void keys16(const uint4& r, unsigned (&k)[8], const _
 
 // The largest non-NaN value of one staged 16-byte vector folded into a running max (NaN inputs are skipped, so a
 // running max that is still NaN has seen no number).
+// Three-input max of sm_100 (max.f32 with three sources): NaN operands are skipped. max3_nan propagates NaN.
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned max_bf16x2(unsigned a, unsigned b) {
+  unsigned d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned max_nan_bf16x2(unsigned a, unsigned b) {
+  unsigned d;
+  asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 __device__ __forceinline__ float vec_max(const uint4& r, float m, const float*) {
-  m = fmaxf(m, __uint_as_float(r.x));
-  m = fmaxf(m, __uint_as_float(r.y));
-  m = fmaxf(m, __uint_as_float(r.z));
-  return fmaxf(m, __uint_as_float(r.w));
+  return max3(max3(m, __uint_as_float(r.x), __uint_as_float(r.y)), __uint_as_float(r.z), __uint_as_float(r.w));
 }
 __device__ __forceinline__ float vec_max(const uint4& r, float m, const __nv_bfloat16*) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&r);
-  const __nv_bfloat162 a = __hmax2(h[0], h[1]), b = __hmax2(h[2], h[3]);
-  const __nv_bfloat162 c = __hmax2(a, b);
-  return fmaxf(m, fmaxf(__low2float(c), __high2float(c)));
+  const unsigned c = max_bf16x2(max_bf16x2(r.x, r.y), max_bf16x2(r.z, r.w));
+  return max3(m, __uint_as_float(c << 16), __uint_as_float(c & 0xffff0000u));
+}
+
+// The largest value of one staged vector with NaN propagating (so a NaN element never hides behind the pre-filter).
+__device__ __forceinline__ float vec_max_nan(const uint4& r, const float*) {
+  return max3_nan(max3_nan(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z)), __uint_as_float(r.w),
+                  __uint_as_float(r.w));
+}
+__device__ __forceinline__ float vec_max_nan(const uint4& r, const __nv_bfloat16*) {
+  const unsigned c = max_nan_bf16x2(max_nan_bf16x2(r.x, r.y), max_nan_bf16x2(r.z, r.w));
+  const float lo = __uint_as_float(c << 16), hi = __uint_as_float(c & 0xffff0000u);
+  return max3_nan(lo, hi, hi);
 }
 
 // The fp32 bits of element e of one staged vector (a bf16 element widened).
@@ -150,48 +185,19 @@ __device__ __forceinline__ unsigned block_suffix_excl(unsigned v, unsigned* warp
   }
   if (lane == 0) warp_tot[warp] = x;
   __syncthreads();
-  unsigned higher = 0;
-  for (int w = warp + 1; w < kWarps; ++w) higher += warp_tot[w];
+  // The warps' totals, suffix-summed across lanes: lane l holds the sum over warps >= l.
+  unsigned t = lane < kWarps ? warp_tot[lane] : 0u;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const unsigned y = __shfl_down_sync(0xffffffffu, t, o);
+    if (lane + o < 32) t += y;
+  }
+  const unsigned higher = __shfl_sync(0xffffffffu, t, (warp + 1) & 31) * (warp + 1 < 32 ? 1u : 0u);
   __syncthreads();
   return higher + x - v;
 }
 
-// Descending bitonic sort of the 32 * P composites held P per lane (element lane * P + p), within one warp.
-template <int P>
-__device__ __forceinline__ void warp_sort_desc(u64 (&v)[P]) {
-  constexpr int N = 32 * P;
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int size = 2; size <= N; size <<= 1) {
-#pragma unroll
-    for (int j = size >> 1; j > 0; j >>= 1) {
-      if (j >= P) {
-#pragma unroll
-        for (int p = 0; p < P; ++p) {
-          const int e = lane * P + p;
-          const u64 o = __shfl_xor_sync(0xffffffffu, v[p], j / P);
-          const bool keep_max = ((e & j) == 0) == ((e & size) == 0);
-          v[p] = keep_max ? (v[p] > o ? v[p] : o) : (v[p] < o ? v[p] : o);
-        }
-      } else {
-#pragma unroll
-        for (int p = 0; p < P; ++p) {
-          if ((p & j) == 0) {
-            const int q = p | j;
-            const int e = lane * P + p;
-            const bool desc = (e & size) == 0;
-            const u64 a = v[p], b = v[q];
-            const bool swap = desc ? a < b : a > b;
-            v[p] = swap ? b : a;
-            v[q] = swap ? a : b;
-          }
-        }
-      }
-    }
-  }
-}
-
-// The bin of a 2^w-bin histogram (w = 10 or 12) that holds the kk-th largest counted item, scanning from the top:
+// The bin of a 2^w-bin histogram (w = 10 or 11) that holds the kk-th largest counted item, scanning from the top:
 // thread t owns bins [t * per, (t + 1) * per). Writes *s_bin and *s_above (the items in higher bins); *s_bin keeps
 // its previous value when fewer than kk items were counted. All threads call it; it ends with a barrier.
 __device__ __forceinline__ void find_bin(const unsigned* hist, int w, unsigned kk, unsigned* warp_tot, int* s_bin,
@@ -223,21 +229,82 @@ __device__ __forceinline__ void collect(const uint4* data, int nv, int n, unsign
     const uint4 r = data[i];
     unsigned mask = vec_not_below(r, f_lo, tag);
     if (mask == 0u) continue;
-    while (mask) {
-      const int e = __ffs(mask) - 1;
-      mask &= mask - 1u;
+    unsigned take = 0u;
+    for (unsigned m = mask; m; m &= m - 1u) {
+      const int e = __ffs(m) - 1;
       const int idx = i * V + e;
-      const u64 c = composite(order_key(elem_bits(r, e, tag)), base_idx + (unsigned)idx);
-      if (idx < n && c >= lo) {
-        const int pos = atomicAdd(s_cnt, 1);
-        if (pos < kCap) cand[pos] = c;
+      if (idx < n && composite(order_key(elem_bits(r, e, tag)), base_idx + (unsigned)idx) >= lo) take |= 1u << e;
+    }
+    if (take == 0u) continue;
+    int pos = atomicAdd(s_cnt, __popc(take));
+    for (; take; take &= take - 1u, ++pos) {
+      const int e = __ffs(take) - 1;
+      if (pos < kCap) cand[pos] = composite(order_key(elem_bits(r, e, tag)), base_idx + (unsigned)(i * V + e));
+    }
+  }
+}
+
+// The same selection into this warp's own slots of the candidate buffer. Two vectors per thread per step; a thread
+// whose vectors all stay below lo (nearly every one) only loads and compares them: no vote, no shuffle. The rare
+// thread holding a candidate reserves its slots with a shared atomic on its warp's own counter (no contention across
+// warps). The counter may pass `slots` (the entries past it are dropped; the caller falls back).
+template <typename T>
+__device__ __forceinline__ void collect_warp(const uint4* data, int nv, int n, unsigned base_idx, u64 lo, u64* region,
+                                             int slots, int* wcount) {
+  constexpr int V = VecN<T>::N;
+  const T* tag = nullptr;
+  const float f_lo = __uint_as_float(key_bits((unsigned)(lo >> 32)));
+  for (int i = threadIdx.x; i < nv; i += 2 * kThreads) {
+    const int i1 = i + kThreads;
+    const uint4 r0 = data[i];
+    const uint4 r1 = i1 < nv ? data[i1] : make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
+    const float m0 = vec_max_nan(r0, tag), m1 = i1 < nv ? vec_max_nan(r1, tag) : -CUDART_INF_F;
+    if (m0 < f_lo && m1 < f_lo) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4 r = h ? r1 : r0;
+      const int iv = h ? i1 : i;
+      if ((h ? m1 : m0) < f_lo) continue;
+      unsigned take = 0u;
+      for (unsigned m = vec_not_below(r, f_lo, tag); m; m &= m - 1u) {
+        const int e = __ffs(m) - 1;
+        const int idx = iv * V + e;
+        if (idx < n && composite(order_key(elem_bits(r, e, tag)), base_idx + (unsigned)idx) >= lo) take |= 1u << e;
+      }
+      if (take == 0u) continue;
+      int pos = atomicAdd(wcount, __popc(take));
+      for (; take; take &= take - 1u, ++pos) {
+        const int e = __ffs(take) - 1;
+        if (pos < slots) region[pos] = composite(order_key(elem_bits(r, e, tag)), base_idx + (unsigned)(iv * V + e));
       }
     }
   }
 }
 
+// The top k of the cnt distinct composites in cand, sorted, into top[0, k) (zero padded when cnt < k): a rank count,
+// G lanes per candidate (G the largest power of two <= 32 with cnt * G <= kThreads), each lane comparing against
+// every G-th candidate, the partial counts summed by xor shuffles. Ends with a barrier.
+__device__ __forceinline__ void select_top(const u64* cand, int cnt, int k, u64* top) {
+  int g = 32;
+  while (g > 1 && cnt * g > kThreads) g >>= 1;
+  const int sub = threadIdx.x & (g - 1);
+  for (int base = 0; base < cnt; base += kThreads / g) {  // uniform trip count: every lane joins the shuffles
+    const int item = base + (int)threadIdx.x / g;
+    u64 c = 0ull;
+    int rank = 0;
+    if (item < cnt) {
+      c = cand[item];
+      for (int j = sub; j < cnt; j += g) rank += cand[j] > c;
+    }
+    for (int o = g >> 1; o > 0; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+    if (item < cnt && sub == 0 && rank < k) top[rank] = c;
+  }
+  for (int e = cnt + threadIdx.x; e < k; e += kThreads) top[e] = 0ull;
+  __syncthreads();
+}
+
 // Radix select over all staged composites: the lower edge `lo` of the digit bin holding the kk-th largest, refined
-// digit by digit (12/10/10 bits of the key, then 12/10/10 of the index) until the composites >= lo fit kCap. Every
+// digit by digit (11/11/10 bits of the key, then 11/11/10 of the index) until the composites >= lo fit kCap. Every
 // level zeroes and rebuilds the histogram. All threads call it, after a barrier that ends all use of `hist`.
 template <typename T>
 __device__ u64 radix_select(const uint4* data, int nv, int n, unsigned base_idx, unsigned kk0, unsigned* hist,
@@ -312,12 +379,12 @@ __global__ void __launch_bounds__(kThreads) topk_chunk(const ChunkArgs a) {
   __shared__ unsigned s_above;
   __shared__ int s_cnt;
   __shared__ int s_last;
+  __shared__ int s_wcnt[kWarps];
 
   const T* tag = nullptr;
   uint4* data = reinterpret_cast<uint4*>(smem_raw);
   unsigned* hist = reinterpret_cast<unsigned*>(smem_raw + a.data_bytes);
   u64* cand = reinterpret_cast<u64*>(hist);  // used only after the last histogram has been read
-  u64* top = reinterpret_cast<u64*>(smem_raw);  // used only after the last pass over the staged chunk
 
   const long long row = blockIdx.y;
   const int nchunks = gridDim.x;
@@ -355,6 +422,7 @@ __global__ void __launch_bounds__(kThreads) topk_chunk(const ChunkArgs a) {
     s_above = 0u;
     s_cnt = 0;
   }
+  if (threadIdx.x < kWarps) s_wcnt[threadIdx.x] = 0;
   __syncthreads();
 
   // 2. A lower bound from the per-thread maxima: the k-th largest of them has at least k elements at or above it, so
@@ -366,61 +434,56 @@ __global__ void __launch_bounds__(kThreads) topk_chunk(const ChunkArgs a) {
     const int v0 = p * pv, v1 = min(nv, v0 + pv);
     if (v1 <= v0) continue;
     if constexpr (kBulk) ok = mbar_wait(&bars[p], 0) && ok;
-    for (int i = v0 + threadIdx.x; i < v1; i += kThreads) fmax = vec_max(data[i], fmax, tag);
+    int i = v0 + threadIdx.x;
+    for (; i + kThreads < v1; i += 2 * kThreads) fmax = vec_max(data[i + kThreads], vec_max(data[i], fmax, tag), tag);
+    if (i < v1) fmax = vec_max(data[i], fmax, tag);
   }
   if (!ok) atomicOr(&g_topk_status, CKB_STATUS_TIMEOUT);
   const unsigned kk0 = (unsigned)min(a.k, n);
   u64 lo = 0;
   if (n > kCap) {
     // fmax is one of this thread's elements (or NaN when it has no number): the maxima counted are real elements.
-    if (fmax == fmax) atomicAdd(&hist[order_key(__float_as_uint(fmax)) >> 20], 1u);
+    if (fmax == fmax) atomicAdd(&hist[order_key(__float_as_uint(fmax)) >> 21], 1u);
     __syncthreads();
-    find_bin(hist, 12, kk0, warp_tot, &s_bin, &s_above);
-    if (s_bin >= 0) lo = (u64)s_bin << 52;
+    find_bin(hist, 11, kk0, warp_tot, &s_bin, &s_above);
+    if (s_bin >= 0) lo = (u64)s_bin << 53;
   }
   __syncthreads();  // the histogram is dead from here: the candidate buffer reuses it
 
-  // 3. Collect the composites >= lo. If they overflow the buffer (heavy ties, or too few maxima), a full radix select
-  //    over the chunk's composites narrows `lo` until they fit, and they are collected again.
-  collect<T>(data, nv, n, base_idx, lo, cand, &s_cnt);
+  // 3. Collect the composites >= lo, each warp into its own kWarpSlots slots (no shared atomics). If a warp's slots
+  //    overflow (heavy ties, or too few maxima), a radix select over the chunk's composites narrows `lo` until they
+  //    fit the whole buffer, and they are collected again.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  collect_warp<T>(data, nv, n, base_idx, lo, cand + warp * kWarpSlots, kWarpSlots, &s_wcnt[warp]);
   __syncthreads();
-  if (s_cnt > kCap) {
+  const int wcnt = s_wcnt[warp];
+  // Every warp scans the 16 counts across its lanes: the total, this warp's start, any overflow.
+  int wc = lane < kWarps ? s_wcnt[lane] : 0;
+  const bool over = __any_sync(0xffffffffu, wc > kWarpSlots);
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, wc, o);
+    if (lane >= o) wc += y;
+  }
+  const int cnt = __shfl_sync(0xffffffffu, wc, 31);
+  const int start = warp ? __shfl_sync(0xffffffffu, wc, (warp - 1) & 31) : 0;
+
+  // 4. The chunk's top k, sorted, into top[0, k) (zero padded when the chunk has fewer than k elements); the chunk's
+  //    staging area is dead from here and holds the packed candidates and top.
+  u64* packed = reinterpret_cast<u64*>(smem_raw);
+  u64* top = packed + kCap;
+  if (!over) {
+    for (int j = lane; j < wcnt; j += 32) packed[start + j] = cand[warp * kWarpSlots + j];
+    __syncthreads();
+    select_top(packed, cnt, a.k, top);
+  } else {
     lo = radix_select<T>(data, nv, n, base_idx, kk0, hist, warp_tot, &s_bin, &s_above);
     if (threadIdx.x == 0) s_cnt = 0;
     __syncthreads();
     collect<T>(data, nv, n, base_idx, lo, cand, &s_cnt);
     __syncthreads();
+    select_top(cand, min(s_cnt, kCap), a.k, top);
   }
-  const int cnt = min(s_cnt, kCap);
-  const int lane = threadIdx.x & 31;
-
-  // 4. The chunk's top k, sorted, into top[0, k) (zero padded when the chunk has fewer than k elements).
-  if (cnt <= kSortMax) {
-    if (threadIdx.x < 32) {
-      u64 v[kSortMax / 32];
-#pragma unroll
-      for (int p = 0; p < kSortMax / 32; ++p) {
-        const int e = lane * (kSortMax / 32) + p;
-        v[p] = e < cnt ? cand[e] : 0ull;
-      }
-      warp_sort_desc<kSortMax / 32>(v);
-#pragma unroll
-      for (int p = 0; p < kSortMax / 32; ++p) {
-        const int e = lane * (kSortMax / 32) + p;
-        if (e < a.k) top[e] = v[p];
-      }
-    }
-    for (int e = kSortMax + threadIdx.x; e < a.k; e += kThreads) top[e] = 0ull;
-  } else {
-    for (int i = threadIdx.x; i < cnt; i += kThreads) {
-      const u64 c = cand[i];
-      int rank = 0;
-      for (int j = 0; j < cnt; ++j) rank += cand[j] > c;
-      if (rank < a.k) top[rank] = c;
-    }
-    for (int e = cnt + threadIdx.x; e < a.k; e += kThreads) top[e] = 0ull;
-  }
-  __syncthreads();
 
   // 5. Output, or the multi-chunk merge by the row's last CTA.
   if (nchunks == 1) {
@@ -428,8 +491,11 @@ __global__ void __launch_bounds__(kThreads) topk_chunk(const ChunkArgs a) {
     return;
   }
   u64* wr = a.work + row * (long long)nchunks * a.k;
-  for (int j = threadIdx.x; j < a.k; j += kThreads) wr[(long long)blockIdx.x * a.k + j] = top[j];
-  __threadfence();
+  // The writers (threads below k <= kThreads) fence their own stores before the row counter moves.
+  if ((int)threadIdx.x < a.k) {
+    wr[(long long)blockIdx.x * a.k + threadIdx.x] = top[threadIdx.x];
+    __threadfence();
+  }
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[row], 1u) == (unsigned)nchunks - 1u;
   __syncthreads();
@@ -499,7 +565,7 @@ long long plan_chunk(long long rows, long long cols, int elem, int min_chunk) {
 
 int data_bytes_for(long long chunk, int elem, int nchunks, int k) {
   long long b = chunk * elem;
-  if (b < (long long)k * 8) b = (long long)k * 8;
+  if (b < (long long)(kCap + k) * 8) b = (long long)(kCap + k) * 8;  // packed candidates + top, after the chunk
   if (nchunks > 1 && b < (long long)nchunks * k * 8) b = (long long)nchunks * k * 8;
   return (int)((b + 127) / 128 * 128);
 }

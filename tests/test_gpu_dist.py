@@ -1,0 +1,87 @@
+"""Multi-GPU paths over NCCL with one process per GPU (skipped with fewer than 2 GPUs):
+  * the vocab-sharded top-k (local shard kernel -> all_gather_into_tensor -> merge kernel) gives every rank the
+    single-GPU answer, bit for bit;
+  * row sharding: each rank normalises its own rows; gathered, they equal the oracle.
+Ranks are spawned processes with a short process-group timeout, so a stuck collective ends the test with an error."""
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    import sys
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    sys.path[:0] = [here, root, os.path.join(root, "cuda-kernels-optimized-for-rtx5090_b200")]
+    import torch.distributed as dist
+
+    from ckb200 import rmsnorm, sharded, workloads
+    from oracle import rmsnorm as orms
+    from oracle import topk as otk
+    from oracle.numerics import to_f32, ulp_distance
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=dev)
+        x = workloads.topk_512x151936(scale=4)["x"]
+        lo, hi = sharded.col_range(x.shape[1], rank, world)
+        values, indices = sharded.topk_vocab_sharded(x[:, lo:hi].contiguous().to(dev), lo, 50)
+        op = sharded.VocabShardedTopK(x.shape[0], 50, device=dev)
+        v2, i2 = op(x[:, lo:hi].contiguous().to(dev), lo)
+        wv, wi = otk.topk(x, 50)
+        ok_topk = (torch.equal(indices.cpu(), wi) and torch.equal(values.cpu(), wv) and
+                   torch.equal(i2.cpu(), wi) and torch.equal(v2.cpu(), wv))
+        inp = workloads.rmsnorm_16384x4096(scale=64)
+        r0, r1 = sharded.row_range(inp["x"].shape[0], rank, world)
+        mine = rmsnorm.rmsnorm(inp["x"][r0:r1].contiguous().to(dev), inp["weight"].to(dev))
+        parts = [torch.empty((sharded.row_range(inp["x"].shape[0], r, world)[1] -
+                              sharded.row_range(inp["x"].shape[0], r, world)[0], 4096),
+                             dtype=torch.bfloat16, device=dev) for r in range(world)]
+        dist.all_gather(parts, mine)
+        full = torch.cat(parts).cpu()
+        ok_rows = int(ulp_distance(to_f32(full), to_f32(orms.rmsnorm(inp["x"], inp["weight"])),
+                                   torch.bfloat16).max()) <= 1
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, bool(ok_topk), bool(ok_rows)))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e), False))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_vocab_sharded_topk_and_row_shards_over_nccl():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        results = [q.get(timeout=300) for _ in range(world)]
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for rank, ok_topk, ok_rows in results:
+        assert ok_topk is True, f"rank {rank}: {ok_topk}"
+        assert ok_rows is True, f"rank {rank}"

@@ -43,7 +43,8 @@ def test_config4_short_rows():
 
 # Column counts that reach every path: group (G = 4, 8, 16, 32), block, cluster (several cluster sizes), and the
 # stream fallback (cols not a multiple of the vector).
-COLS = [1, 4, 12, 16, 32, 100, 128, 256, 512, 1024, 2048, 8192, 16384, 20000, 65536, 100000, 262144, 1048576,
+COLS = [1, 4, 12, 16, 32, 100, 128, 256, 512, 1024, 2048, 8192, 16384, 20000, 32768, 65536, 100000, 262144,
+        1048576, 4194304,
         13, 1001, 40001]
 
 
@@ -67,14 +68,15 @@ def test_misaligned(cols):
     _check(x, softmax.softmax(xd), f"misaligned {cols}")
 
 
-@pytest.mark.parametrize("cols", [128, 8192, 262144])
+@pytest.mark.parametrize("cols", [128, 8192, 262144, 4194304])
 def test_special_values(cols):
-    x = torch.randn(5, cols, generator=torch.Generator().manual_seed(2))
+    x = torch.randn(6, cols, generator=torch.Generator().manual_seed(2))
     x[0, 3] = float("-inf")
     x[1, :] = float("-inf")
     x[2, 5] = float("inf")
     x[3, 9] = float("nan")
     x[4, :] = 0.0
+    x[5, : cols // 2] = float("-inf")  # whole cluster slices of -inf beside finite ones
     _check(x, softmax.softmax(x.cuda()), f"special {cols}")
 
 

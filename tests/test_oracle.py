@@ -134,9 +134,11 @@ def test_rope_cpu_baseline_agrees_with_oracle():
 
 # ------------------------------------------------------------------------------------------------------- topk ----
 def test_topk_oracle_matches_reference_kernel():
-    """Bit-exact on every row of finite values. The reference's contract covers finite inputs (topk/kernel.cu:15);
-    on the one fixture row holding a NaN its kernel left the NaN out, while the oracle (and ckb200) rank a positive
-    NaN above +inf as the documented composite order does: that row must equal the oracle on the row without it."""
+    """Bit-exact on every row of finite values. The reference's contract covers finite inputs (topk/kernel.cu:15).
+    Its fp32 kernel, built for sm_100a and run on a B200, returns a positive NaN as -0.0 and ranks it there (so a
+    random row's top 50 never holds it), while the oracle and ckb200 rank a positive NaN above +inf as the documented
+    composite order does (and as the reference's own bf16 path does): the fixture row holding a NaN must equal the
+    oracle on that row with the NaN left out."""
     z = _load("topk.npz")
     for i in range(4):
         dt = torch.bfloat16 if int(z[f"dtype{i}"]) == 1 else torch.float32

@@ -46,7 +46,18 @@ def test_matches_launch_on_two_calls_in_a_row(dtype, scale):
 
 
 def test_rejects_plans_beyond_the_scratch():
+    """512 rows x 1M columns split into tens of chunks per row: 512 * chunks * 50 composites of workspace, more than
+    the scratch holds (launch() with a caller's workspace serves it). Real buffers are passed so that even a planner
+    change could not make the call touch memory it does not own."""
     fn = _noalloc()
-    # 512 rows x 4M columns needs 512 * 342 * 50 composites of workspace, far beyond the 4 MiB scratch; the check
-    # happens before anything touches the (never read) pointers.
-    assert fn(None, None, None, 512, 1 << 22, 50, 0, None) == -2
+    rows, cols, k = 512, 1 << 20, 50
+    x = torch.empty(rows, cols, device="cuda")
+    v = torch.empty(rows, k, device="cuda")
+    i = torch.empty(rows, k, dtype=torch.int64, device="cuda")
+    plan = ctypes.CDLL(build.lib_path("topk")).plan
+    plan.restype = ctypes.c_longlong
+    plan.argtypes = [ctypes.c_longlong, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    nseg = -(-cols // plan(rows, cols, 0, 256, 4, 2048))
+    assert nseg > 1 and rows * nseg * k > 491520
+    assert fn(x.data_ptr(), v.data_ptr(), i.data_ptr(), rows, cols, k, 0, torch.cuda.current_stream().cuda_stream) == -2
+    torch.cuda.synchronize()
