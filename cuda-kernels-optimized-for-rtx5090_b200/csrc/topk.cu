@@ -6,23 +6,23 @@
 // the same total order as the reference's pack() (topk/kernel.cu:56-60): larger value first, equal values by lower
 // index, NaN above +inf, -NaN below -inf. The top k of a row are its k largest composites.
 //
-// Algorithm (one CTA per chunk of a row, 512 threads):
-//   1. the chunk is pulled into shared memory by bulk copies (cp.async.bulk, several pieces on their own mbarriers);
-//   2. a lower bound: each thread keeps the max of its numbers (one fmax per element as the pieces land); the k-th
-//      largest of those maxima has at least k elements at or above it, so the lower edge of its bin in a 2048-bin
-//      histogram of the maxima's top 11 key bits (found by a block suffix scan) bounds the chunk's k-th largest key
-//      from below;
-//   3. one pass collects the composites at or above that edge (typically k + a few dozen): a float compare per
-//      element, and the composite only for the few that pass, appended by each warp into its own slots of the
-//      candidate buffer (a warp prefix sum places them; no shared atomics). If a warp's slots overflow (heavy ties),
-//      a radix select over the composites narrows the edge first: the digit bin holding the k-th largest, refined
-//      digit by digit (11/11/10 bits of the key, 11/11/10 of the index, so value ties resolve by index) until the
-//      composites at or above it fit the 1024-entry buffer;
-//   4. a block rank count (several lanes per candidate) leaves the chunk's top k sorted;
-//   5. a row split over several chunks writes each chunk's sorted top k to the workspace; the row's last CTA to finish
-//      (per-row counter, reset by that CTA) merges the sorted lists by rank (binary search of every candidate in the
-//      other lists) and decodes values and indices from the composites (x is not read again).
-// The vocab-sharded variant runs steps 1-5 on a column shard with a global column offset and stops at the sorted
+// Algorithm (grid: segments x rows, 512 threads per CTA, one pass over HBM):
+//   1. each CTA streams its segment of the row through a ring of shared-memory stages that its threads fill with
+//      16-byte asynchronous copies (cp.async); a thread reads back only the vectors it copied itself, so the ring
+//      needs no block barrier and keeps several tiles (512 x U vectors each) in flight;
+//   2. first tile, a lower bound: every thread takes the max of its numbers; in each warp the c-th largest of the 32
+//      maxima (c = ceil(k / 16)) has c distinct elements at or above it, so the smallest of the 16 warps' values has
+//      at least k elements at or above it and bounds the segment's k-th largest composite from below;
+//   3. every tile: the composites at or above the running bound are appended (a float pre-filter per vector, the
+//      composite only for the few that pass) behind the running top k in a candidate buffer; a block rank count leaves
+//      the new running top k and the bound rises to one above its k-th entry, so a later tile passes only elements
+//      that enter the top k (about k / tile number of them). A tile that overflows the buffer (heavy ties) first
+//      raises the bound by a radix select over its composites, still in registers (11/11/10 bits of the key, then
+//      11/11/10 of the index, so value ties resolve by index);
+//   4. a row split over several segments writes each segment's sorted top k to the workspace; the row's last CTA to
+//      finish (per-row counter, reset by that CTA) merges the lists pairwise (each entry's rank in the partner list by
+//      binary search) and decodes values and indices from the composites (x is not read again).
+// The vocab-sharded variant runs steps 1-4 on a column shard with a global column offset and stops at the sorted
 // composites; after an all-gather across GPUs the merge kernel ranks the per-GPU lists the same way.
 #include "ckb200_topk.h"
 #include "common.cuh"
@@ -39,28 +39,75 @@ namespace {
 
 typedef unsigned long long u64;
 
-#ifndef CKB_TOPK_THREADS
-#define CKB_TOPK_THREADS 512
+// Two CTA shapes. 256 threads (8 warps, 4 CTAs per SM) serve k <= 256: a GPU's worth of CTAs holds 592 rows'
+// streams at once, so a batch of a few hundred long rows runs in one wave without splitting rows. 512 threads (16
+// warps, 2 CTAs per SM) serve k <= 512. The first tile's bound needs c = ceil(k / warps) <= 32 maxima per warp.
+#ifndef CKB_TOPK_STAGES
+#define CKB_TOPK_STAGES 3
 #endif
-constexpr int kThreads = CKB_TOPK_THREADS;
-constexpr int kWarps = kThreads / 32;
-constexpr int kBins = 2048;            // largest digit: 11 bits
-constexpr int kCap = 1024;             // candidate buffer (aliases the histogram)
-constexpr int kWarpSlots = kCap / kWarps;  // each warp appends into its own slice of the candidate buffer
+#ifndef CKB_TOPK_UNROLL
+#define CKB_TOPK_UNROLL 4
+#endif
+#ifndef CKB_TOPK_STAGES_256
+#define CKB_TOPK_STAGES_256 4
+#endif
+#ifndef CKB_TOPK_UNROLL_256
+#define CKB_TOPK_UNROLL_256 2
+#endif
+#ifndef CKB_TOPK_WIDE_ONLY
+#define CKB_TOPK_WIDE_ONLY 0
+#endif
+constexpr int kCand = 1024;                       // running top k + survivors since the last compaction
+constexpr int kPack = 512;                        // compaction scratch: select output, packing, 1024-bin histogram
+#ifndef CKB_TOPK_SPEC_MARGIN
+#define CKB_TOPK_SPEC_MARGIN 12
+#endif
+#ifndef CKB_TOPK_SPEC_SCALE
+#define CKB_TOPK_SPEC_SCALE 1.0f
+#endif
+// Speculative bound after a compaction: the m-th largest composite seen, m = ceil(scale * k * fraction seen) + margin.
+// With i.i.d. values the segment's count above it is about m / fraction seen; falling short of k needs a Gamma(m)
+// variable below k * fraction, which the margin makes rare (and the kernel checks for it anyway).
+constexpr int kSpecMargin = CKB_TOPK_SPEC_MARGIN;
+constexpr float kSpecScale = CKB_TOPK_SPEC_SCALE;
 constexpr int kMaxK = 512;
-constexpr int kPieces = 4;
-constexpr int kLevels = 6;
-#ifndef CKB_TOPK_CHUNK_BYTES
-#define CKB_TOPK_CHUNK_BYTES (96 * 1024)
-#endif
-constexpr int kChunkBytes = CKB_TOPK_CHUNK_BYTES;  // staged bytes per CTA: chunk + histogram keep 2 CTAs per SM
-constexpr int kMaxDataBytes = 160 * 1024;
+constexpr int kDirectSelect = 192;                // compactions of more candidates narrow them by radix first
+constexpr int kRadixBins = 1024;                  // 10-bit digits
+constexpr int kLevels = 7;                        // 6 x 10 bits + 4 bits cover the 64-bit composite
+constexpr int kSlots = 12;                        // survivor vectors a warp records between compactions
+constexpr int kSlotsFull = 8;                     // a warp holding this many asks for a compaction
+constexpr int kSmPerSmBytes = 233472;             // shared memory per SM (228 KB)
 
-// Radix digits over the 64-bit composite, most significant first: 11/11/10 bits of the key, then 11/11/10 of ~index.
-__device__ __forceinline__ int level_shift(int L) {
-  return L == 0 ? 53 : L == 1 ? 42 : L == 2 ? 32 : L == 3 ? 21 : L == 4 ? 10 : 0;
-}
-__device__ __forceinline__ int level_width(int L) { return (L == 2 || L == 5) ? 10 : 11; }
+template <int NT>
+struct Cfg {
+  static constexpr int kWarps = NT / 32;
+  static constexpr int kMaxK = NT == 512 ? 512 : 256;              // c = ceil(k / kWarps) <= 32
+  static constexpr int kStages = NT == 512 ? CKB_TOPK_STAGES : CKB_TOPK_STAGES_256;  // ring depth
+  static constexpr int kU = NT == 512 ? CKB_TOPK_UNROLL : CKB_TOPK_UNROLL_256;      // vectors per thread per tile
+  static constexpr int kTileVecs = NT * kU;       // thread t holds vectors u * NT + t of a tile
+  static constexpr int kRingBytes = kStages * kTileVecs * 16;
+  static constexpr int kSlotBytes = kWarps * kSlots * 20;  // recorded vectors (16 bytes) and indices (4 bytes)
+  static constexpr int kSmemBytes = kRingBytes + kCand * 8 + kPack * 8 + kSlotBytes;
+  static constexpr int kMergeEntries = kRingBytes / 16;    // nseg * k: the merge ping-pongs between ring halves
+  static constexpr int kMinBlocks = NT == 512 ? 2 : 4;
+  static constexpr int kCtasPerSm =
+      kSmPerSmBytes / (kSmemBytes + 2048) < kMinBlocks ? kSmPerSmBytes / (kSmemBytes + 2048) : kMinBlocks;
+  static_assert(kMaxK <= 32 * kWarps, "the first tile's bound needs ceil(k / warps) <= 32");
+  static_assert(kCand - kMaxK >= kMaxK, "after a compaction a radix select must leave room for k survivors");
+  static_assert(kMergeEntries >= kMaxK, "the ring must hold one list per segment");
+  static_assert(kRadixBins % NT == 0, "histogram bins split evenly over the threads");
+  static_assert(kCtasPerSm >= 1, "one CTA's shared memory fits an SM");
+};
+// Segments per row that every k fits in either shape's merge.
+constexpr int kMaxSeg = Cfg<256>::kMergeEntries / Cfg<256>::kMaxK < Cfg<512>::kMergeEntries / Cfg<512>::kMaxK
+                            ? Cfg<256>::kMergeEntries / Cfg<256>::kMaxK
+                            : Cfg<512>::kMergeEntries / Cfg<512>::kMaxK;
+static_assert(kRadixBins * 4 <= kPack * 8, "the radix histogram lives in the compaction scratch");
+static_assert(kSlots <= 32, "a warp expands its slots one per lane");
+
+// Radix digits over the 64-bit composite, most significant first: six of 10 bits, then the last 4.
+__device__ __forceinline__ int level_shift(int L) { return L < 6 ? 54 - 10 * L : 0; }
+__device__ __forceinline__ int level_width(int L) { return L < 6 ? 10 : 4; }
 
 __device__ __forceinline__ unsigned order_key(unsigned bits) {
   return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
@@ -70,21 +117,6 @@ __device__ __forceinline__ unsigned key_bits(unsigned key) {  // inverse of orde
 }
 __device__ __forceinline__ u64 composite(unsigned key, unsigned idx) { return ((u64)key << 32) | (u64)(~idx); }
 
-// Keys of the elements in one 16-byte vector of staged data.
-__device__ __forceinline__ void keys16(const uint4& r, unsigned (&k)[4], const float*) {
-  k[0] = order_key(r.x); k[1] = order_key(r.y); k[2] = order_key(r.z); k[3] = order_key(r.w);
-}
-__device__ __forceinline__ void keys16(const uint4& r, unsigned (&k)[8], const __nv_bfloat16*) {
-  const unsigned w[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    k[2 * j] = order_key(w[j] << 16);
-    k[2 * j + 1] = order_key(w[j] & 0xffff0000u);
-  }
-}
-
-// The largest non-NaN value of one staged 16-byte vector folded into a running max (NaN inputs are skipped, so a
-// running max that is still NaN has seen no number).
 // Three-input max of sm_100 (max.f32 with three sources): NaN operands are skipped. max3_nan propagates NaN.
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
@@ -107,6 +139,8 @@ __device__ __forceinline__ unsigned max_nan_bf16x2(unsigned a, unsigned b) {
   return d;
 }
 
+// The largest non-NaN value of one 16-byte vector folded into a running max (NaN inputs are skipped, so a running
+// max that is still NaN has seen no number). The result is always one of the inputs.
 __device__ __forceinline__ float vec_max(const uint4& r, float m, const float*) {
   return max3(max3(m, __uint_as_float(r.x), __uint_as_float(r.y)), __uint_as_float(r.z), __uint_as_float(r.w));
 }
@@ -115,7 +149,7 @@ __device__ __forceinline__ float vec_max(const uint4& r, float m, const __nv_bfl
   return max3(m, __uint_as_float(c << 16), __uint_as_float(c & 0xffff0000u));
 }
 
-// The largest value of one staged vector with NaN propagating (so a NaN element never hides behind the pre-filter).
+// The largest value of one vector with NaN propagating (so a NaN element never hides behind the pre-filter).
 __device__ __forceinline__ float vec_max_nan(const uint4& r, const float*) {
   return max3_nan(max3_nan(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z)), __uint_as_float(r.w),
                   __uint_as_float(r.w));
@@ -126,7 +160,8 @@ __device__ __forceinline__ float vec_max_nan(const uint4& r, const __nv_bfloat16
   return max3_nan(lo, hi, hi);
 }
 
-// The fp32 bits of element e of one staged vector (a bf16 element widened).
+// The fp32 bits of element e of one vector (a bf16 element widened). Selects, not an indexed array, so the vector
+// stays in registers.
 __device__ __forceinline__ unsigned word_of(const uint4& r, int j) {
   return j < 2 ? (j == 0 ? r.x : r.y) : (j == 2 ? r.z : r.w);
 }
@@ -135,9 +170,11 @@ __device__ __forceinline__ unsigned elem_bits(const uint4& r, int e, const __nv_
   const unsigned w = word_of(r, e >> 1);
   return (e & 1) ? (w & 0xffff0000u) : (w << 16);
 }
+__device__ __forceinline__ unsigned scalar_bits(float v) { return __float_as_uint(v); }
+__device__ __forceinline__ unsigned scalar_bits(__nv_bfloat16 v) { return (unsigned)__bfloat16_as_ushort(v) << 16; }
 
-// Bit mask (bit e) of the elements of one staged vector that are not below f_lo as floats, NaN included: a superset
-// of the elements whose order key is >= the key of f_lo.
+// Bit mask (bit e) of the elements of one vector that are not below f_lo as floats, NaN included: a superset of the
+// elements whose order key is >= the key of f_lo.
 __device__ __forceinline__ unsigned vec_not_below(const uint4& r, float f_lo, const float*) {
   return (unsigned)!(__uint_as_float(r.x) < f_lo) | ((unsigned)!(__uint_as_float(r.y) < f_lo) << 1) |
          ((unsigned)!(__uint_as_float(r.z) < f_lo) << 2) | ((unsigned)!(__uint_as_float(r.w) < f_lo) << 3);
@@ -174,7 +211,16 @@ __device__ __forceinline__ int count_greater(const u64* list, int n, u64 c) {
   return lo;
 }
 
-// Sum of v over the threads with a higher threadIdx.x (all threads call it; two barriers).
+// ------------------------------------------------------------------------------------ asynchronous 16-byte copies ---
+__device__ __forceinline__ void cp_async16(void* dst_smem, const void* src) {
+  asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(smem_u32(dst_smem)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Sum of v over the threads with a higher threadIdx.x (all NT threads call it; two barriers).
+template <int NT>
 __device__ __forceinline__ unsigned block_suffix_excl(unsigned v, unsigned* warp_tot) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   unsigned x = v;
@@ -186,7 +232,7 @@ __device__ __forceinline__ unsigned block_suffix_excl(unsigned v, unsigned* warp
   if (lane == 0) warp_tot[warp] = x;
   __syncthreads();
   // The warps' totals, suffix-summed across lanes: lane l holds the sum over warps >= l.
-  unsigned t = lane < kWarps ? warp_tot[lane] : 0u;
+  unsigned t = lane < NT / 32 ? warp_tot[lane] : 0u;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const unsigned y = __shfl_down_sync(0xffffffffu, t, o);
@@ -197,19 +243,23 @@ __device__ __forceinline__ unsigned block_suffix_excl(unsigned v, unsigned* warp
   return higher + x - v;
 }
 
-// The bin of a 2^w-bin histogram (w = 10 or 11) that holds the kk-th largest counted item, scanning from the top:
-// thread t owns bins [t * per, (t + 1) * per). Writes *s_bin and *s_above (the items in higher bins); *s_bin keeps
-// its previous value when fewer than kk items were counted. All threads call it; it ends with a barrier.
-__device__ __forceinline__ void find_bin(const unsigned* hist, int w, unsigned kk, unsigned* warp_tot, int* s_bin,
+// The bin of an nb-bin histogram (nb a power of two <= 1024) that holds the kk-th largest counted item, scanning
+// from the top: thread t owns bins [t * per, (t + 1) * per). Writes *s_bin and *s_above (the items in higher bins);
+// *s_bin keeps its previous value when fewer than kk items were counted. All threads call it; it ends with a barrier.
+template <int NT>
+__device__ __forceinline__ void find_bin(const unsigned* hist, int nb, unsigned kk, unsigned* warp_tot, int* s_bin,
                                          unsigned* s_above) {
-  const int per = (1 << w) / kThreads;
+  const int per = nb > NT ? nb / NT : 1;
+  const int b0 = threadIdx.x * per;
   unsigned mine = 0;
-  for (int b = 0; b < per; ++b) mine += hist[threadIdx.x * per + b];
-  unsigned run = block_suffix_excl(mine, warp_tot);
+  for (int b = 0; b < per; ++b)
+    if (b0 + b < nb) mine += hist[b0 + b];
+  unsigned run = block_suffix_excl<NT>(mine, warp_tot);
   for (int b = per - 1; b >= 0; --b) {
-    const unsigned h = hist[threadIdx.x * per + b];
+    if (b0 + b >= nb) continue;
+    const unsigned h = hist[b0 + b];
     if (run < kk && run + h >= kk) {
-      *s_bin = threadIdx.x * per + b;
+      *s_bin = b0 + b;
       *s_above = run;
     }
     run += h;
@@ -217,148 +267,275 @@ __device__ __forceinline__ void find_bin(const unsigned* hist, int w, unsigned k
   __syncthreads();
 }
 
-// Appends every staged composite >= lo to cand (at most kCap stored, *s_cnt counts them all). A float compare finds
-// the few elements that may qualify; only those build their composite and take a slot with a shared atomic.
-template <typename T>
-__device__ __forceinline__ void collect(const uint4* data, int nv, int n, unsigned base_idx, u64 lo, u64* cand,
-                                        int* s_cnt) {
+// Reserves n consecutive slots for each lane of the warp: an exclusive scan of n over the lanes and one shared
+// atomic on *counter for the whole warp. Every lane of the warp calls it; returns this lane's first slot.
+__device__ __forceinline__ int warp_reserve(int n, int* counter) {
+  const int lane = threadIdx.x & 31;
+  int incl = n;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  int base = 0;
+  if (lane == 31 && incl > 0) base = atomicAdd(counter, incl);
+  base = __shfl_sync(0xffffffffu, base, 31);
+  return base + incl - n;
+}
+
+// One tile of the stream as this thread holds it: U vectors (vector u is the segment's vector vb + u * NT, present
+// when below nv) and, on the first tile only, one element outside the aligned body.
+template <typename T, int NT, int U>
+struct TileRegs {
+  uint4 r[U];
+  int vb, nv;
+  unsigned base_idx;  // column index of the segment's first body element
+  bool has_x;
+  unsigned xbits, xidx;
+};
+
+// Calls f(c) for every composite >= lo of this thread's tile.
+template <typename T, int NT, int U, typename F>
+__device__ __forceinline__ void for_each_at_least(const TileRegs<T, NT, U>& t, u64 lo, F&& f) {
+  constexpr int V = VecN<T>::N;
+  const T* tag = nullptr;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int v = t.vb + u * NT;
+    if (v >= t.nv) continue;
+    const unsigned idx0 = t.base_idx + (unsigned)(v * V);
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const u64 c = composite(order_key(elem_bits(t.r[u], e, tag)), idx0 + (unsigned)e);
+      if (c >= lo) f(c);
+    }
+  }
+  if (t.has_x) {
+    const u64 c = composite(order_key(t.xbits), t.xidx);
+    if (c >= lo) f(c);
+  }
+}
+
+// Appends the tile's composites >= lo to buf[off + ...] (entries past kCand are dropped; *counter counts them all).
+// A float compare per vector finds the few that may qualify; only those build their composites, and a warp that has
+// any reserves its slots with one shared atomic. Every lane of every warp calls it.
+template <typename T, int NT, int U>
+__device__ __forceinline__ void collect(const TileRegs<T, NT, U>& t, u64 lo, u64* buf, int off, int* counter) {
   constexpr int V = VecN<T>::N;
   const T* tag = nullptr;
   const float f_lo = __uint_as_float(key_bits((unsigned)(lo >> 32)));
-  for (int i = threadIdx.x; i < nv; i += kThreads) {
-    const uint4 r = data[i];
-    unsigned mask = vec_not_below(r, f_lo, tag);
-    if (mask == 0u) continue;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int v = t.vb + u * NT;
+    const bool maybe = v < t.nv && !(vec_max_nan(t.r[u], tag) < f_lo);
+    if (!__any_sync(0xffffffffu, maybe)) continue;
+    const unsigned idx0 = t.base_idx + (unsigned)(v * V);
     unsigned take = 0u;
-    for (unsigned m = mask; m; m &= m - 1u) {
-      const int e = __ffs(m) - 1;
-      const int idx = i * V + e;
-      if (idx < n && composite(order_key(elem_bits(r, e, tag)), base_idx + (unsigned)idx) >= lo) take |= 1u << e;
-    }
-    if (take == 0u) continue;
-    int pos = atomicAdd(s_cnt, __popc(take));
+    if (maybe)
+      for (unsigned m = vec_not_below(t.r[u], f_lo, tag); m; m &= m - 1u) {
+        const int e = __ffs(m) - 1;
+        if (composite(order_key(elem_bits(t.r[u], e, tag)), idx0 + (unsigned)e) >= lo) take |= 1u << e;
+      }
+    int pos = off + warp_reserve(__popc(take), counter);
     for (; take; take &= take - 1u, ++pos) {
       const int e = __ffs(take) - 1;
-      if (pos < kCap) cand[pos] = composite(order_key(elem_bits(r, e, tag)), base_idx + (unsigned)(i * V + e));
+      if (pos < kCand) buf[pos] = composite(order_key(elem_bits(t.r[u], e, tag)), idx0 + (unsigned)e);
     }
+  }
+  if (__any_sync(0xffffffffu, t.has_x)) {
+    const u64 c = composite(order_key(t.xbits), t.xidx);
+    const bool keep = t.has_x && c >= lo;
+    const int pos = off + warp_reserve(keep ? 1 : 0, counter);
+    if (keep && pos < kCand) buf[pos] = c;
   }
 }
 
-// The same selection into this warp's own slots of the candidate buffer. Two vectors per thread per step; a thread
-// whose vectors all stay below lo (nearly every one) only loads and compares them: no vote, no shuffle. The rare
-// thread holding a candidate reserves its slots with a shared atomic on its warp's own counter (no contention across
-// warps). The counter may pass `slots` (the entries past it are dropped; the caller falls back).
-template <typename T>
-__device__ __forceinline__ void collect_warp(const uint4* data, int nv, int n, unsigned base_idx, u64 lo, u64* region,
-                                             int slots, int* wcount) {
-  constexpr int V = VecN<T>::N;
+// Records, for tiles after the first, each of this thread's vectors that may hold a composite >= lo (its largest value
+// not below f_lo, NaN included) in its warp's slots: the vector and its index within the segment, at a place found
+// by a ballot (no atomics, no composites; those are built when the slots are expanded). Returns the warp's new count;
+// slots past kSlots are not written (the caller sees the count exceed kSlots). Every lane of the warp calls it.
+template <typename T, int NT, int U>
+__device__ __forceinline__ int record(const TileRegs<T, NT, U>& t, float f_lo, uint4* wslot, unsigned* widx,
+                                      int wcnt) {
   const T* tag = nullptr;
-  const float f_lo = __uint_as_float(key_bits((unsigned)(lo >> 32)));
-  for (int i = threadIdx.x; i < nv; i += 2 * kThreads) {
-    const int i1 = i + kThreads;
-    const uint4 r0 = data[i];
-    const uint4 r1 = i1 < nv ? data[i1] : make_uint4(0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu);
-    const float m0 = vec_max_nan(r0, tag), m1 = i1 < nv ? vec_max_nan(r1, tag) : -CUDART_INF_F;
-    if (m0 < f_lo && m1 < f_lo) continue;
+  const unsigned below = (1u << (threadIdx.x & 31)) - 1u;
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint4 r = h ? r1 : r0;
-      const int iv = h ? i1 : i;
-      if ((h ? m1 : m0) < f_lo) continue;
-      unsigned take = 0u;
-      for (unsigned m = vec_not_below(r, f_lo, tag); m; m &= m - 1u) {
-        const int e = __ffs(m) - 1;
-        const int idx = iv * V + e;
-        if (idx < n && composite(order_key(elem_bits(r, e, tag)), base_idx + (unsigned)idx) >= lo) take |= 1u << e;
-      }
-      if (take == 0u) continue;
-      int pos = atomicAdd(wcount, __popc(take));
-      for (; take; take &= take - 1u, ++pos) {
-        const int e = __ffs(take) - 1;
-        if (pos < slots) region[pos] = composite(order_key(elem_bits(r, e, tag)), base_idx + (unsigned)(iv * V + e));
+  for (int u = 0; u < U; ++u) {
+    const int v = t.vb + u * NT;
+    const bool maybe = v < t.nv && !(vec_max_nan(t.r[u], tag) < f_lo);
+    const unsigned bal = __ballot_sync(0xffffffffu, maybe);
+    if (bal == 0u) continue;
+    if (maybe) {
+      const int pos = wcnt + __popc(bal & below);
+      if (pos < kSlots) {
+        wslot[pos] = t.r[u];
+        widx[pos] = (unsigned)v;
       }
     }
+    wcnt += __popc(bal);
   }
+  return wcnt;
 }
 
-// The top k of the cnt distinct composites in cand, sorted, into top[0, k) (zero padded when cnt < k): a rank count,
-// G lanes per candidate (G the largest power of two <= 32 with cnt * G <= kThreads), each lane comparing against
-// every G-th candidate, the partial counts summed by xor shuffles. Ends with a barrier.
-__device__ __forceinline__ void select_top(const u64* cand, int cnt, int k, u64* top) {
-  int g = 32;
-  while (g > 1 && cnt * g > kThreads) g >>= 1;
-  const int sub = threadIdx.x & (g - 1);
-  for (int base = 0; base < cnt; base += kThreads / g) {  // uniform trip count: every lane joins the shuffles
-    const int item = base + (int)threadIdx.x / g;
-    u64 c = 0ull;
-    int rank = 0;
-    if (item < cnt) {
-      c = cand[item];
-      for (int j = sub; j < cnt; j += g) rank += cand[j] > c;
-    }
-    for (int o = g >> 1; o > 0; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
-    if (item < cnt && sub == 0 && rank < k) top[rank] = c;
-  }
-  for (int e = cnt + threadIdx.x; e < k; e += kThreads) top[e] = 0ull;
-  __syncthreads();
-}
-
-// Radix select over all staged composites: the lower edge `lo` of the digit bin holding the kk-th largest, refined
-// digit by digit (11/11/10 bits of the key, then 11/11/10 of the index) until the composites >= lo fit kCap. Every
-// level zeroes and rebuilds the histogram. All threads call it, after a barrier that ends all use of `hist`.
+// Appends the composites >= lo of this warp's n recorded vectors (n <= kSlots, one per lane) to buf[off + ...]
+// (entries past kCand are dropped; *counter counts them all); with buf null it only counts them. Every lane of the
+// warp calls it.
 template <typename T>
-__device__ u64 radix_select(const uint4* data, int nv, int n, unsigned base_idx, unsigned kk0, unsigned* hist,
-                            unsigned* warp_tot, int* s_bin, unsigned* s_above) {
+__device__ __forceinline__ void expand(const uint4* wslot, const unsigned* widx, int n, unsigned base_idx, u64 lo,
+                                       u64* buf, int off, int* counter) {
   constexpr int V = VecN<T>::N;
   const T* tag = nullptr;
-  u64 prefix = 0, lo = 0;
-  unsigned kk = kk0, above_total = 0;
+  const int lane = threadIdx.x & 31;
+  uint4 r = make_uint4(0u, 0u, 0u, 0u);
+  unsigned idx0 = 0u, take = 0u;
+  if (lane < n) {
+    r = wslot[lane];
+    idx0 = base_idx + widx[lane] * (unsigned)V;
+#pragma unroll
+    for (int e = 0; e < V; ++e)
+      if (composite(order_key(elem_bits(r, e, tag)), idx0 + (unsigned)e) >= lo) take |= 1u << e;
+  }
+  if (buf == nullptr) {
+    const int sum = __reduce_add_sync(0xffffffffu, __popc(take));
+    if (lane == 0 && sum > 0) atomicAdd(counter, sum);
+    return;
+  }
+  int pos = off + warp_reserve(__popc(take), counter);
+  for (; take; take &= take - 1u, ++pos) {
+    const int e = __ffs(take) - 1;
+    if (pos < kCand) buf[pos] = composite(order_key(elem_bits(r, e, tag)), idx0 + (unsigned)e);
+  }
+}
+
+// Calls f(c) for every composite >= lo of this warp's n recorded vectors (one per lane).
+template <typename T, typename F>
+__device__ __forceinline__ void for_each_recorded(const uint4* wslot, const unsigned* widx, int n, unsigned base_idx,
+                                                  u64 lo, F&& f) {
+  constexpr int V = VecN<T>::N;
+  const T* tag = nullptr;
+  const int lane = threadIdx.x & 31;
+  if (lane >= n) return;
+  const uint4 r = wslot[lane];
+  const unsigned idx0 = base_idx + widx[lane] * (unsigned)V;
+#pragma unroll
+  for (int e = 0; e < V; ++e) {
+    const u64 c = composite(order_key(elem_bits(r, e, tag)), idx0 + (unsigned)e);
+    if (c >= lo) f(c);
+  }
+}
+
+// Radix select: the lower edge of the digit bin holding the kk-th largest of the items that each thread's
+// items(f) visits, refined digit by digit (10 bits at a time from the top of the composite, so value ties resolve by
+// index) until the items >= edge number at most cap (cap >= kk: the last digit leaves exactly kk). Every level
+// rebuilds the histogram `hist` (kRadixBins words). All threads call it; it ends with a barrier.
+template <int NT, typename Items>
+__device__ u64 radix_edge(Items&& items, unsigned kk, int cap, unsigned* hist, unsigned* warp_tot, int* s_bin,
+                          unsigned* s_above) {
+  u64 prefix = 0, edge = 0;
+  unsigned above_total = 0;
   for (int L = 0; L < kLevels; ++L) {
     const int sh = level_shift(L), w = level_width(L);
     const unsigned mask = (1u << w) - 1u;
-    for (int i = threadIdx.x; i < kBins; i += kThreads) hist[i] = 0u;
+    for (int i = threadIdx.x; i < kRadixBins; i += NT) hist[i] = 0u;
+    if (threadIdx.x == 0) *s_bin = 0;
     __syncthreads();
-    for (int i = threadIdx.x; i < nv; i += kThreads) {
-      unsigned key[V];
-      keys16(data[i], key, tag);
-#pragma unroll
-      for (int e = 0; e < V; ++e) {
-        const int idx = i * V + e;
-        if (idx < n) {
-          const u64 c = composite(key[e], base_idx + (unsigned)idx);
-          if (L == 0 || (c >> (sh + w)) == prefix) atomicAdd(&hist[(unsigned)(c >> sh) & mask], 1u);
-        }
-      }
-    }
+    items([&](u64 c) {
+      if (L == 0 || (c >> (sh + w)) == prefix) atomicAdd(&hist[(unsigned)(c >> sh) & mask], 1u);
+    });
     __syncthreads();
-    find_bin(hist, w, kk, warp_tot, s_bin, s_above);
+    find_bin<NT>(hist, 1 << w, kk, warp_tot, s_bin, s_above);
     const int bin = *s_bin;
     const unsigned above = *s_above, inbin = hist[bin];
     const u64 next = (prefix << w) | (u64)bin;
-    lo = next << sh;
-    if (above_total + above + inbin <= (unsigned)kCap || L == kLevels - 1) break;
+    edge = next << sh;
+    if (above_total + above + inbin <= (unsigned)cap || L == kLevels - 1) break;
     above_total += above;
     kk -= above;
     prefix = next;
     __syncthreads();  // every thread has read hist[bin] and the bin before the next level rewrites them
   }
-  return lo;
+  __syncthreads();  // the histogram is dead before the caller reuses its buffer
+  return edge;
 }
 
-struct ChunkArgs {
+// The top k of the cnt distinct composites in cand, sorted, into top[0, k) (zero padded when cnt < k): a rank count,
+// G lanes per candidate (G the largest power of two <= 32 with cnt * G <= kThreads), each lane comparing against
+// every G-th candidate, the partial counts summed by xor shuffles. Ends with a barrier.
+template <int NT>
+__device__ __forceinline__ void select_top(const u64* cand, int cnt, int k, u64* top) {
+  int g = 32;
+  while (g > 1 && cnt * g > NT) g >>= 1;
+  const int sub = threadIdx.x & (g - 1);
+  for (int base = 0; base < cnt; base += NT / g) {  // uniform trip count: every lane joins the shuffles
+    const int item = base + (int)threadIdx.x / g;
+    u64 c = 0ull;
+    int rank = 0;
+    if (item < cnt) {
+      c = cand[item];
+#pragma unroll 4
+      for (int j = sub; j < cnt; j += g) rank += cand[j] > c;
+    }
+    for (int o = g >> 1; o > 0; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+    if (item < cnt && sub == 0 && rank < k) top[rank] = c;
+  }
+  for (int e = cnt + threadIdx.x; e < k; e += NT) top[e] = 0ull;
+  __syncthreads();
+}
+
+// Compaction: the top k of the n distinct composites in cand[0, n), sorted, into cand[0, k) (zero padded when
+// n < k); returns min(k, n). Up to cap = max(k + 32, kDirectSelect) candidates (at most kPack) go straight to the
+// rank count, whose cost grows with the square of the count; more are first narrowed by a radix select to at most
+// cap, packed into tmp. tmp (kPack entries) is scratch. All threads call it; ends with a barrier.
+template <int NT>
+__device__ int compact(u64* cand, int n, int k, u64* tmp, unsigned* warp_tot, int* s_bin, unsigned* s_above,
+                       int* s_pack) {
+  const int cap = min(kPack, max(kDirectSelect, k + 32));
+  if (n <= cap) {
+    select_top<NT>(cand, n, k, tmp);
+    for (int i = threadIdx.x; i < k; i += NT) cand[i] = tmp[i];
+    __syncthreads();
+    return min(k, n);
+  }
+  const u64 edge = radix_edge<NT>(
+      [&](auto&& f) {
+        for (int i = threadIdx.x; i < n; i += NT) f(cand[i]);
+      },
+      (unsigned)k, cap, reinterpret_cast<unsigned*>(tmp), warp_tot, s_bin, s_above);
+  if (threadIdx.x == 0) *s_pack = 0;
+  __syncthreads();
+  for (int base = 0; base < n; base += NT) {  // uniform trip count: every lane joins warp_reserve
+    const int i = base + threadIdx.x;
+    const u64 c = i < n ? cand[i] : 0ull;
+    const bool keep = i < n && c >= edge;
+    const int pos = warp_reserve(keep ? 1 : 0, s_pack);
+    if (keep && pos < kPack) tmp[pos] = c;
+  }
+  __syncthreads();
+  select_top<NT>(tmp, min(*s_pack, kPack), k, cand);
+  return min(k, n);
+}
+
+// The bound after a compaction that left a full top k: one above its k-th entry (every composite that can still
+// enter is larger), never below the bound already in force.
+__device__ __forceinline__ u64 raise_bound(u64 lo, u64 kth) {
+  const u64 b = kth == ~0ull ? kth : kth + 1ull;
+  return b > lo ? b : lo;
+}
+
+struct SegArgs {
   const void* x;
   void* values;          // mode 0: [rows, k] in x's dtype
   long long* indices;    // mode 0: [rows, k]
   u64* lists;            // mode 1: [rows, k] sorted composites, zero padded
-  u64* work;             // [rows, nchunks, k] when a row has several chunks
+  u64* work;             // [rows, nseg, k] when a row has several segments
   unsigned* counters;    // [rows], zero on entry, left zero
   long long col_offset;  // added to every column index
-  int cols, chunk, k, data_bytes, mode;
+  int cols, k, mode;
 };
 
-// Writes the row's final top k (sorted composites top[0, k)) in the requested form.
+// Writes entry j of the row's final top k in the requested form.
 template <typename T>
-__device__ __forceinline__ void emit(const ChunkArgs& a, long long row, int j, u64 c) {
+__device__ __forceinline__ void emit(const SegArgs& a, long long row, int j, u64 c) {
   if (a.mode == 0) {
     reinterpret_cast<T*>(a.values)[row * a.k + j] = decode_value<T>(c);
     a.indices[row * a.k + j] = decode_index(c);
@@ -367,154 +544,281 @@ __device__ __forceinline__ void emit(const ChunkArgs& a, long long row, int j, u
   }
 }
 
-// Grid (nchunks, rows). kBulk: the chunk's rows are 16-byte aligned and sized, so bulk copies stage it; otherwise the
-// threads copy it element by element.
-template <typename T, bool kBulk>
-__global__ void __launch_bounds__(kThreads) topk_chunk(const ChunkArgs a) {
+// Grid (nseg, rows). A row's 16-byte aligned body is split evenly into nseg segments of vectors; the elements before
+// the body's first aligned address go with segment 0, those after its end with the last segment.
+template <typename T, int NT>
+__global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const SegArgs a) {
+  using C = Cfg<NT>;
   constexpr int V = VecN<T>::N;
+  constexpr int kThreads = NT, kWarps = C::kWarps, kU = C::kU, kStages = C::kStages, kTileVecs = C::kTileVecs;
+  constexpr int kRingBytes = C::kRingBytes, kMergeEntries = C::kMergeEntries;
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  __shared__ __align__(8) uint64_t bars[kPieces];
   __shared__ unsigned warp_tot[kWarps];
+  __shared__ unsigned warp_key[kWarps];
   __shared__ int s_bin;
   __shared__ unsigned s_above;
-  __shared__ int s_cnt;
+  __shared__ int s_cnt;     // appends of the current collect or expansion
+  __shared__ int s_flag[3];  // tile j >= 1: bit 0 some warp's slots are half full, bit 1 some warp's overflowed
+  __shared__ int s_pack;
   __shared__ int s_last;
-  __shared__ int s_wcnt[kWarps];
 
   const T* tag = nullptr;
-  uint4* data = reinterpret_cast<uint4*>(smem_raw);
-  unsigned* hist = reinterpret_cast<unsigned*>(smem_raw + a.data_bytes);
-  u64* cand = reinterpret_cast<u64*>(hist);  // used only after the last histogram has been read
+  uint4* ring = reinterpret_cast<uint4*>(smem_raw);
+  u64* cand = reinterpret_cast<u64*>(smem_raw + kRingBytes);  // running top at [0, ntop), survivors behind it
+  u64* tmp = cand + kCand;  // compaction scratch: kPack composites or the radix histogram
+  unsigned char* slots = smem_raw + kRingBytes + (kCand + kPack) * 8;
+  uint4* wslot = reinterpret_cast<uint4*>(slots) + (threadIdx.x >> 5) * kSlots;  // this warp's recorded vectors
+  unsigned* widx = reinterpret_cast<unsigned*>(slots + kWarps * kSlots * 16) + (threadIdx.x >> 5) * kSlots;
 
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long long row = blockIdx.y;
-  const int nchunks = gridDim.x;
-  const long long begin = (long long)blockIdx.x * a.chunk;
-  const int n = (int)min((long long)a.chunk, (long long)a.cols - begin);
-  const T* src = reinterpret_cast<const T*>(a.x) + row * a.cols + begin;
-  const int nv = (n + V - 1) / V;  // staged 16-byte vectors
-  const int pv = (nv + kPieces - 1) / kPieces;
-  const unsigned base_idx = (unsigned)(a.col_offset + begin);
+  const int seg = blockIdx.x, nseg = gridDim.x, k = a.k;
+  const T* rowp = reinterpret_cast<const T*>(a.x) + row * (long long)a.cols;
 
-  // 1. Stage the chunk; zero the histogram meanwhile.
-  if constexpr (kBulk) {
-    if (threadIdx.x == 0) {
+  // The row's aligned body [head, tail0) in vectors, and this segment's share [v0, v0 + nv).
+  const int mis = (int)((reinterpret_cast<uintptr_t>(rowp) & 15u) / sizeof(T));
+  const int head = mis ? min(a.cols, V - mis) : 0;
+  const int nvr = (a.cols - head) / V;
+  const int tail0 = head + nvr * V;
+  const int segv = (nvr + nseg - 1) / nseg;
+  const int v0 = min(nvr, seg * segv);
+  const int nv = min(nvr, v0 + segv) - v0;
+  const uint4* body = reinterpret_cast<const uint4*>(rowp + head) + v0;
+
+  TileRegs<T, NT, kU> t;
+  t.nv = nv;
+  t.base_idx = (unsigned)(a.col_offset + head) + (unsigned)v0 * (unsigned)V;
+  const int nhead = seg == 0 ? head : 0;
+  const int nextra = nhead + (seg == nseg - 1 ? a.cols - tail0 : 0);  // at most 2 (V - 1)
+  const bool mine_x = tid < nextra;
+  t.xbits = 0u;
+  t.xidx = 0u;
+  if (mine_x) {
+    const int col = tid < nhead ? tid : tail0 + (tid - nhead);
+    t.xbits = scalar_bits(rowp[col]);
+    t.xidx = (unsigned)(a.col_offset + col);
+  }
+
+  const int ntiles = max(1, (nv + kTileVecs - 1) / kTileVecs);
+  // Tile j's vectors of this thread into stage j % kStages; one commit group per tile (empty past the last tile).
+  auto issue = [&](int j) {
+    if (j < ntiles) {
+      uint4* st = ring + (j % kStages) * kTileVecs;
 #pragma unroll
-      for (int p = 0; p < kPieces; ++p) mbar_init(&bars[p], 1);
-      mbar_fence_init();
-#pragma unroll
-      for (int p = 0; p < kPieces; ++p) {
-        const int v0 = p * pv, v1 = min(nv, v0 + pv);
-        if (v1 > v0) {
-          mbar_arrive_expect_tx(&bars[p], (unsigned)(v1 - v0) * 16u);
-          bulk_load(data + v0, reinterpret_cast<const uint4*>(src) + v0, (unsigned)(v1 - v0) * 16u, &bars[p]);
+      for (int u = 0; u < kU; ++u) {
+        const int v = j * kTileVecs + u * kThreads + tid;
+        if (v < nv) cp_async16(st + u * kThreads + tid, body + v);
+      }
+    }
+    cp_async_commit();
+  };
+
+  // Pass 0 speculates: the bound rises to the m-th largest composite seen so far (m sized so that the whole segment
+  // almost surely holds k composites above it). The answer is exact when the final k-th composite reaches every
+  // speculative bound used (then no element left out can rank in the top k); otherwise pass 1 streams the segment
+  // again with guaranteed bounds only.
+  const float seg_elems = (float)nv * V + (float)nextra;
+  int ntop = 0;    // entries of the running top in cand[0, ntop), sorted
+  int filled = 0;  // survivors appended behind it since the last compaction
+  u64 lo = 0;      // every composite that can still enter the top k (or, speculating, pass the check) is >= lo
+  u64 spec = 0;    // the highest speculative bound used
+  bool speculate = true;
+
+  // Appends the current collect's or expansion's count (all threads call it, after the appends and a barrier).
+  auto take_count = [&]() {
+    filled = min(filled + s_cnt, kCand - ntop);
+    __syncthreads();  // every thread has read s_cnt before the next reset
+  };
+  // The top k of cand, a guaranteed bound from its k-th entry and, speculating, a speculative one from its m-th
+  // (after `seen` elements of the segment).
+  auto compact_all = [&](float seen) {  // seen < 0: no speculative bound
+    ntop = compact<NT>(cand, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
+    filled = 0;
+    if (ntop == k) {
+      lo = raise_bound(lo, cand[k - 1]);
+      if (speculate && seen >= 0.0f) {
+        const int m = (int)ceilf(kSpecScale * (float)k * seen) + kSpecMargin;
+        if (m < k) {
+          const u64 s_m = cand[m - 1];
+          spec = s_m > spec ? s_m : spec;
+          lo = s_m > lo ? s_m : lo;
         }
       }
     }
-  } else {
-    T* d = reinterpret_cast<T*>(data);
-    for (int i = threadIdx.x; i < n; i += kThreads) d[i] = src[i];
-    // Pad the last vector with NaN: the max pass skips it and the collect pass rejects it by index.
-    for (int i = n + threadIdx.x; i < nv * V; i += kThreads) d[i] = from_f32<T>(__int_as_float(0x7fc00000));
-  }
-  for (int i = threadIdx.x; i < kBins / 4; i += kThreads) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0u, 0u, 0u, 0u);
-  if (threadIdx.x == 0) {
-    s_bin = -1;
-    s_above = 0u;
-    s_cnt = 0;
-  }
-  if (threadIdx.x < kWarps) s_wcnt[threadIdx.x] = 0;
-  __syncthreads();
-
-  // 2. A lower bound from the per-thread maxima: the k-th largest of them has at least k elements at or above it, so
-  //    the lower edge of its histogram bin bounds the chunk's k-th largest key from below. Only 512 maxima touch the
-  //    histogram; the one pass over the chunk is a max.
-  bool ok = true;
-  float fmax = __int_as_float(0x7fc00000);  // NaN: no number seen yet
-  for (int p = 0; p < kPieces; ++p) {
-    const int v0 = p * pv, v1 = min(nv, v0 + pv);
-    if (v1 <= v0) continue;
-    if constexpr (kBulk) ok = mbar_wait(&bars[p], 0) && ok;
-    int i = v0 + threadIdx.x;
-    for (; i + kThreads < v1; i += 2 * kThreads) fmax = vec_max(data[i + kThreads], vec_max(data[i], fmax, tag), tag);
-    if (i < v1) fmax = vec_max(data[i], fmax, tag);
-  }
-  if (!ok) atomicOr(&g_topk_status, CKB_STATUS_TIMEOUT);
-  const unsigned kk0 = (unsigned)min(a.k, n);
-  u64 lo = 0;
-  if (n > kCap) {
-    // fmax is one of this thread's elements (or NaN when it has no number): the maxima counted are real elements.
-    if (fmax == fmax) atomicAdd(&hist[order_key(__float_as_uint(fmax)) >> 21], 1u);
+  };
+  // The composites >= lo of the tile held in registers into cand; a tile that overflows the buffer (heavy ties, rising
+  // values) first compacts what is there and raises lo until its composites fit.
+  auto collect_tile = [&]() {
+    if (tid == 0) s_cnt = 0;
     __syncthreads();
-    find_bin(hist, 11, kk0, warp_tot, &s_bin, &s_above);
-    if (s_bin >= 0) lo = (u64)s_bin << 53;
-  }
-  __syncthreads();  // the histogram is dead from here: the candidate buffer reuses it
+    collect(t, lo, cand, ntop + filled, &s_cnt);
+    __syncthreads();
+    if (ntop + filled + s_cnt > kCand) {
+      __syncthreads();  // every thread has read s_cnt
+      ntop = compact<NT>(cand, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
+      filled = 0;
+      if (ntop == k) lo = raise_bound(lo, cand[k - 1]);
+      const u64 edge = radix_edge<NT>([&](auto&& f) { for_each_at_least(t, lo, f); }, (unsigned)k, kCand - ntop,
+                                  reinterpret_cast<unsigned*>(tmp), warp_tot, &s_bin, &s_above);
+      lo = edge > lo ? edge : lo;
+      if (tid == 0) s_cnt = 0;
+      __syncthreads();
+      collect(t, lo, cand, ntop, &s_cnt);
+      __syncthreads();
+    }
+    take_count();
+  };
+  // Every warp's first n recorded vectors (n per warp) into cand. Their composites >= lo are counted first; when they
+  // do not fit, cand is compacted, and if they still do not fit (heavy ties) lo rises by a radix select over them.
+  auto expand_all = [&](int n) {
+    n = min(n, kSlots);
+    if (ntop + filled + kWarps * kSlots * V <= kCand) {  // every composite of every slot fits: no count needed
+      if (tid == 0) s_cnt = 0;
+      __syncthreads();
+      expand<T>(wslot, widx, n, t.base_idx, lo, cand, ntop + filled, &s_cnt);
+      __syncthreads();
+      take_count();
+      return;
+    }
+    if (tid == 0) s_cnt = 0;
+    __syncthreads();
+    expand<T>(wslot, widx, n, t.base_idx, lo, nullptr, 0, &s_cnt);
+    __syncthreads();
+    const int need = s_cnt;
+    __syncthreads();
+    if (need == 0) return;
+    if (ntop + filled + need > kCand) compact_all(-1.0f);
+    if (ntop + filled + need > kCand) {
+      const u64 edge = radix_edge<NT>(
+          [&](auto&& f) { for_each_recorded<T>(wslot, widx, n, t.base_idx, lo, f); }, (unsigned)k, kCand - ntop,
+          reinterpret_cast<unsigned*>(tmp), warp_tot, &s_bin, &s_above);
+      lo = edge > lo ? edge : lo;
+    }
+    if (tid == 0) s_cnt = 0;
+    __syncthreads();
+    expand<T>(wslot, widx, n, t.base_idx, lo, cand, ntop + filled, &s_cnt);
+    __syncthreads();
+    take_count();
+  };
 
-  // 3. Collect the composites >= lo, each warp into its own kWarpSlots slots (no shared atomics). If a warp's slots
-  //    overflow (heavy ties, or too few maxima), a radix select over the chunk's composites narrows `lo` until they
-  //    fit the whole buffer, and they are collected again.
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  collect_warp<T>(data, nv, n, base_idx, lo, cand + warp * kWarpSlots, kWarpSlots, &s_wcnt[warp]);
-  __syncthreads();
-  const int wcnt = s_wcnt[warp];
-  // Every warp scans the 16 counts across its lanes: the total, this warp's start, any overflow.
-  int wc = lane < kWarps ? s_wcnt[lane] : 0;
-  const bool over = __any_sync(0xffffffffu, wc > kWarpSlots);
+  for (int pass = 0; pass < 2; ++pass) {
+    speculate = pass == 0;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, wc, o);
-    if (lane >= o) wc += y;
-  }
-  const int cnt = __shfl_sync(0xffffffffu, wc, 31);
-  const int start = warp ? __shfl_sync(0xffffffffu, wc, (warp - 1) & 31) : 0;
+    for (int j = 0; j < kStages - 1; ++j) issue(j);
+    for (int i = tid; i < k; i += kThreads) cand[i] = 0ull;
+    if (tid < 3) s_flag[tid] = 0;
+    ntop = 0;
+    filled = 0;
+    lo = 0;
+    spec = 0;
+    int wcnt = 0;  // this warp's recorded vectors
+    for (int j = 0; j < ntiles; ++j) {
+      issue(j + kStages - 1);
+      cp_async_wait<kStages - 1>();  // this thread's copies of tile j have landed
+      const uint4* st = ring + (j % kStages) * kTileVecs + tid;
+      t.vb = j * kTileVecs + tid;
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        t.r[u] = t.vb + u * kThreads < nv ? st[u * kThreads]
+                                           : make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
+      t.has_x = j == 0 && mine_x;
+      const float seen = ((float)min(nv, (j + 1) * kTileVecs) * V + (float)nextra) / seg_elems;
 
-  // 4. The chunk's top k, sorted, into top[0, k) (zero padded when the chunk has fewer than k elements); the chunk's
-  //    staging area is dead from here and holds the packed candidates and top.
-  u64* packed = reinterpret_cast<u64*>(smem_raw);
-  u64* top = packed + kCap;
-  if (!over) {
-    for (int j = lane; j < wcnt; j += 32) packed[start + j] = cand[warp * kWarpSlots + j];
-    __syncthreads();
-    select_top(packed, cnt, a.k, top);
-  } else {
-    lo = radix_select<T>(data, nv, n, base_idx, kk0, hist, warp_tot, &s_bin, &s_above);
-    if (threadIdx.x == 0) s_cnt = 0;
-    __syncthreads();
-    collect<T>(data, nv, n, base_idx, lo, cand, &s_cnt);
-    __syncthreads();
-    select_top(cand, min(s_cnt, kCap), a.k, top);
+      if (j == 0) {
+        // The bound: c-th largest per-thread maximum of each warp (key 0 when a thread saw no number), smallest over
+        // the warps. Key 0 is no number's key, so a warp short of c numbers leaves the bound at 0: no bound.
+        float fm = __int_as_float(0x7fc00000);
+#pragma unroll
+        for (int u = 0; u < kU; ++u) fm = vec_max(t.r[u], fm, tag);
+        if (t.has_x) fm = max3(fm, __uint_as_float(t.xbits), __uint_as_float(t.xbits));
+        // A bitonic sort of the 32 keys across the lanes, descending: lane l ends with the (l + 1)-th largest.
+        unsigned key = fm == fm ? order_key(__float_as_uint(fm)) : 0u;
+#pragma unroll
+        for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+          for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            const unsigned o = __shfl_xor_sync(0xffffffffu, key, stride);
+            const bool keep_max = ((lane & stride) == 0) == ((lane & size) == 0);
+            key = keep_max ? max(key, o) : min(key, o);
+          }
+        }
+        const unsigned wk = __shfl_sync(0xffffffffu, key, (k + kWarps - 1) / kWarps - 1);
+        if (lane == 0) warp_key[warp] = wk;
+        __syncthreads();
+        unsigned b = warp_key[0];
+#pragma unroll
+        for (int w = 1; w < kWarps; ++w) b = min(b, warp_key[w]);
+        lo = (u64)b << 32;
+        collect_tile();
+        compact_all(seen);
+        continue;
+      }
+
+      // Later tiles: record the vectors that may hold a survivor; expand and compact only when a warp's slots fill.
+      const int before = wcnt;
+      wcnt = record(t, __uint_as_float(key_bits((unsigned)(lo >> 32))), wslot, widx, wcnt);
+      if (lane == 0 && wcnt >= kSlotsFull) atomicOr(&s_flag[j % 3], wcnt > kSlots ? 3 : 1);
+      if (tid == 0) s_flag[(j + 1) % 3] = 0;  // its last reads came before the barrier of tile j - 1
+      __syncthreads();
+      const int flag = s_flag[j % 3];
+      if (flag & 2) {
+        // Some warp overflowed: keep every warp's records from earlier tiles, take this tile from registers.
+        expand_all(before);
+        wcnt = 0;
+        collect_tile();
+        compact_all(seen);
+      } else if (flag & 1) {
+        expand_all(wcnt);
+        wcnt = 0;
+        if (filled > 0) compact_all(seen);
+      }
+    }
+    expand_all(wcnt);
+    if (filled > 0) ntop = compact<NT>(cand, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
+    cp_async_wait<0>();
+    if (spec == 0ull || (ntop == k && cand[k - 1] >= spec)) break;
+    __syncthreads();  // every thread has read cand[k - 1] before the second pass clears the buffer
   }
 
-  // 5. Output, or the multi-chunk merge by the row's last CTA.
-  if (nchunks == 1) {
-    for (int j = threadIdx.x; j < a.k; j += kThreads) emit<T>(a, row, j, top[j]);
+  // Output, or the multi-segment merge by the row's last CTA.
+  if (nseg == 1) {
+    for (int i = tid; i < k; i += kThreads) emit<T>(a, row, i, cand[i]);
     return;
   }
-  u64* wr = a.work + row * (long long)nchunks * a.k;
+  u64* wr = a.work + ((long long)row * nseg + seg) * k;
   // The writers (threads below k <= kThreads) fence their own stores before the row counter moves.
-  if ((int)threadIdx.x < a.k) {
-    wr[(long long)blockIdx.x * a.k + threadIdx.x] = top[threadIdx.x];
+  if (tid < k) {
+    wr[tid] = cand[tid];
     __threadfence();
   }
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[row], 1u) == (unsigned)nchunks - 1u;
+  if (tid == 0) s_last = atomicAdd(&a.counters[row], 1u) == (unsigned)nseg - 1u;
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const int total = nchunks * a.k;
-  u64* lists = reinterpret_cast<u64*>(smem_raw);
-  for (int i = threadIdx.x; i < total; i += kThreads) lists[i] = __ldcg(wr + i);
+  u64* la = reinterpret_cast<u64*>(smem_raw);  // the ring is idle: two halves of nseg * k <= kMergeEntries each
+  u64* lb = la + kMergeEntries;
+  const u64* rw = a.work + (long long)row * nseg * k;
+  for (int i = tid; i < nseg * k; i += kThreads) la[i] = __ldcg(rw + i);
   __syncthreads();
-  for (int i = threadIdx.x; i < total; i += kThreads) {
-    const u64 c = lists[i];
-    if (c == 0ull) continue;
-    const int own = i / a.k;
-    int rank = i - own * a.k;
-    for (int l = 0; l < nchunks && rank < a.k; ++l)
-      if (l != own) rank += count_greater(lists + l * a.k, a.k, c);
-    if (rank < a.k) emit<T>(a, row, rank, c);
+  // Pairwise rounds: lists 2p and 2p + 1 become list p (an odd last list moves on as it is). An entry's place in the
+  // merged list is its place in its own list plus the entries of the partner list above it; zero padding lands
+  // behind every real entry.
+  for (int n = nseg; n > 1; n = (n + 1) / 2) {
+    for (int i = tid; i < n * k; i += kThreads) {
+      const int l = i / k, e = i - l * k;
+      const u64 c = la[i];
+      int rank = e;
+      if (!((n & 1) && l == n - 1)) rank += count_greater(la + (l ^ 1) * k, k, c);
+      if (rank < k) lb[(l >> 1) * k + rank] = c;
+    }
+    __syncthreads();
+    u64* sw = la;
+    la = lb;
+    lb = sw;
   }
-  if (threadIdx.x == 0) a.counters[row] = 0u;
+  for (int i = tid; i < k; i += kThreads) emit<T>(a, row, i, la[i]);
+  if (tid == 0) a.counters[row] = 0u;
 }
 
 // Merge of nlists sorted composite lists per row, lists laid out [nlists][rows][k] (an all-gather's output); one
@@ -544,65 +848,86 @@ __global__ void __launch_bounds__(256) topk_merge(const u64* __restrict__ lists,
   }
 }
 
-// Columns per CTA: the fewest chunks whose staged bytes fit kChunkBytes, raised (down to min_chunk columns, up to
-// kGrowChunks chunks so the last CTA's merge stays short) until the grid holds at least three CTAs per SM; a multiple
-// of 16 columns so every chunk starts 16-byte aligned.
-constexpr long long kGrowChunks = 32;
+// The CTA shape for k: 256 threads whenever k fits that shape's bound, else 512.
+inline bool narrow_for(int k) { return !CKB_TOPK_WIDE_ONLY && k <= Cfg<256>::kMaxK; }
+constexpr int kPlanShape = CKB_TOPK_WIDE_ONLY ? 512 : 256;  // the shape plan() assumes (k <= 256)
 
-long long plan_chunk(long long rows, long long cols, int elem, int min_chunk) {
+// Segments per row: the count (1 .. kMaxSeg, each at least min_chunk columns) with the least modelled time. CTAs run
+// in waves of kCtasPerSm per SM; while the GPU is full each CTA streams at the HBM bandwidth's share of one slot,
+// otherwise at what its own ring keeps in flight (kStages - 1 tiles per load latency). A CTA also pays a fixed start
+// (first tile's latency, the bound) and a split row one merge round per halving of its lists.
+constexpr double kHbmBytesPerNs = 6500.0;
+constexpr double kLoadLatencyNs = 1500.0;
+constexpr double kCtaFixedNs = 600.0;
+constexpr double kMergeRoundNs = 300.0;
+
+long long plan_seg(long long rows, long long cols, int elem, int min_chunk) {
+  using C = Cfg<kPlanShape>;
   if (rows <= 0 || cols <= 0) return cols > 0 ? cols : 1;
-  const long long max_elems = kChunkBytes / elem;
-  long long nchunks = (cols + max_elems - 1) / max_elems;
-  const long long target = 3LL * device_sm_count();
   if (min_chunk < 1024) min_chunk = 1024;
-  while (rows * nchunks < target && nchunks < kGrowChunks && (cols + nchunks) / (nchunks + 1) >= min_chunk)
-    ++nchunks;
-  if (nchunks <= 1) return cols;
-  long long chunk = (cols + nchunks - 1) / nchunks;
-  chunk = (chunk + 15) / 16 * 16;
-  return chunk;
-}
-
-int data_bytes_for(long long chunk, int elem, int nchunks, int k) {
-  long long b = chunk * elem;
-  if (b < (long long)(kCap + k) * 8) b = (long long)(kCap + k) * 8;  // packed candidates + top, after the chunk
-  if (nchunks > 1 && b < (long long)nchunks * k * 8) b = (long long)nchunks * k * 8;
-  return (int)((b + 127) / 128 * 128);
-}
-
-template <typename T>
-int start_chunk(const ChunkArgs& base, long long rows, long long cols, long long chunk, cudaStream_t s) {
-  const int elem = (int)sizeof(T);
-  const long long nchunks = (cols + chunk - 1) / chunk;
-  ChunkArgs a = base;
-  a.cols = (int)cols;
-  a.chunk = (int)chunk;
-  a.data_bytes = data_bytes_for(chunk, elem, (int)nchunks, a.k);
-  if (a.data_bytes > kMaxDataBytes) return -1;
-  const int smem = a.data_bytes + kBins * 4;
-  const bool bulk = aligned16(a.x) && (cols * elem) % 16 == 0 && (chunk * elem) % 16 == 0;
-  const dim3 grid((unsigned)nchunks, (unsigned)rows);
-  if (bulk) {
-    auto kern = topk_chunk<T, true>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return (int)cudaGetLastError();
-    kern<<<grid, kThreads, smem, s>>>(a);
-  } else {
-    auto kern = topk_chunk<T, false>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return (int)cudaGetLastError();
-    kern<<<grid, kThreads, smem, s>>>(a);
+  const long long slots = (long long)device_sm_count() * C::kCtasPerSm;
+  const double cta_bw = (double)(C::kStages - 1) * C::kTileVecs * 16 / kLoadLatencyNs;
+  long long best_n = 1;
+  double best = 0.0;
+  for (long long n = 1; n <= kMaxSeg; ++n) {
+    if (n > 1 && cols / n < min_chunk) break;
+    const long long ctas = rows * n;
+    const long long active = ctas < slots ? ctas : slots;
+    double bw = kHbmBytesPerNs / (double)active;
+    if (bw > cta_bw) bw = cta_bw;
+    const long long waves = (ctas + slots - 1) / slots;
+    int rounds = 0;
+    for (long long m = n; m > 1; m = (m + 1) / 2) ++rounds;
+    const double ns = (double)waves * ((double)cols * elem / (double)n / bw + kCtaFixedNs) + rounds * kMergeRoundNs;
+    if (n == 1 || ns < best) {
+      best = ns;
+      best_n = n;
+    }
   }
+  return (cols + best_n - 1) / best_n;
+}
+
+// Sets the kernel's shared-memory limit once per device.
+template <typename T, int NT>
+cudaError_t prepare_stream_kernel() {
+  static std::atomic<unsigned long long> done{0ull};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(topk_stream<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<NT>::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return cudaSuccess;
+}
+
+template <typename T, int NT>
+int start_shape(const SegArgs& a, long long rows, long long nseg, cudaStream_t s) {
+  const cudaError_t e = prepare_stream_kernel<T, NT>();
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return (int)e;
+  }
+  topk_stream<T, NT><<<dim3((unsigned)nseg, (unsigned)rows), NT, Cfg<NT>::kSmemBytes, s>>>(a);
   return (int)cudaGetLastError();
 }
 
-// The reference's argument checks (topk/kernel.cu:551-554) plus this library's chunk staging limit.
-bool bad_args(long long rows, long long cols, int k, long long chunk, int elem) {
+template <typename T>
+int start_seg(const SegArgs& a, long long rows, long long nseg, cudaStream_t s) {
+  return narrow_for(a.k) ? start_shape<T, 256>(a, rows, nseg, s) : start_shape<T, 512>(a, rows, nseg, s);
+}
+
+long long segments(long long cols, long long chunk) { return (cols + chunk - 1) / chunk; }
+
+// The reference's argument checks (topk/kernel.cu:551-554) plus this library's limits: an element-aligned x and
+// at most the shape's merge capacity (segments x k composites) for a split row.
+bool bad_args(const void* x, long long rows, long long cols, int k, long long chunk, int elem) {
   if (k > cols || k > kMaxK || cols > INT_MAX / 2 || rows > 65535 || chunk <= 0) return true;
-  const long long nchunks = (cols + chunk - 1) / chunk;
-  if (nchunks > 1 && (chunk % 4 || nchunks * k > INT_MAX / 2)) return true;
+  if (reinterpret_cast<uintptr_t>(x) % (uintptr_t)elem) return true;
   if (chunk > cols) chunk = cols;
-  return data_bytes_for(chunk, elem, (int)nchunks, k) > kMaxDataBytes;
+  const long long cap = narrow_for(k) ? Cfg<256>::kMergeEntries : Cfg<512>::kMergeEntries;
+  return segments(cols, chunk) * k > cap;
 }
 
 }  // namespace
@@ -612,30 +937,30 @@ using namespace ckb;
 
 // Replaces the reference's top-k `plan` (topk/kernel.cu:520-547): the columns per CTA for a rows x cols launch
 // (dtype 0 fp32, 1 bf16). `threads` and `depth` are the reference's kernel knobs and do not change the B200 plan;
-// min_chunk is a lower bound on the chunk when a row is split to fill the GPU. A row's chunk count is
-// ceil(cols / chunk); the workspace launch() needs is rows * chunks * k int64 values.
+// min_chunk is a lower bound on the columns per CTA when a row is split. A row's segment count is
+// ceil(cols / chunk); the workspace launch() needs is rows * segments * k int64 values.
 CKB_EXPORT long long plan(long long rows, long long cols, int dtype, int threads, int depth, int min_chunk) {
   (void)threads;
   (void)depth;
-  return plan_chunk(rows, cols, dtype == kBF16 ? 2 : 4, min_chunk);
+  return plan_seg(rows, cols, dtype == kBF16 ? 2 : 4, min_chunk);
 }
 
 // Replaces the reference's top-k `launch` (topk/kernel.cu:549-570): same arguments, checks and return codes. work is
-// int64 [rows * nchunks * k] (unused with one chunk), counters int32 [rows] zeroed once and left zeroed by the kernel.
-// `chunk` must come from plan() (or be small enough for the shared-memory staging; larger gives -1).
+// int64 [rows * segments * k] (unused with one segment), counters int32 [rows] zeroed once and left zeroed by the
+// kernel. Any chunk >= 1 is served while segments * k <= 6144 (larger gives -1); plan() gives the fastest.
 CKB_EXPORT int launch(const void* x, void* values, void* indices, void* work, void* counters, long long rows,
                       long long cols, int k, int dtype, int threads, int depth, long long chunk,
                       cudaStream_t stream) {
   if (rows <= 0 || k <= 0) return 0;
   if (threads != 128 && threads != 256 && threads != 512) return -1;
   if (depth != 2 && depth != 4 && depth != 8) return -1;
+  if (dtype != kF32 && dtype != kBF16) return -1;
   const int elem = dtype == kBF16 ? 2 : 4;
-  if (bad_args(rows, cols, k, chunk, elem)) return -1;
+  if (bad_args(x, rows, cols, k, chunk, elem)) return -1;
   if (chunk > cols) chunk = cols;
-  ChunkArgs a{x, values, (long long*)indices, nullptr, (u64*)work, (unsigned*)counters, 0, 0, 0, k, 0, 0};
-  if (dtype == kF32) return start_chunk<float>(a, rows, cols, chunk, stream);
-  if (dtype == kBF16) return start_chunk<__nv_bfloat16>(a, rows, cols, chunk, stream);
-  return -1;
+  const SegArgs a{x, values, (long long*)indices, nullptr, (u64*)work, (unsigned*)counters, 0, (int)cols, k, 0};
+  if (dtype == kF32) return start_seg<float>(a, rows, segments(cols, chunk), stream);
+  return start_seg<__nv_bfloat16>(a, rows, segments(cols, chunk), stream);
 }
 
 // Top-k of a column shard for the vocab-sharded variant (no counterpart in the reference): x is [rows, cols] holding
@@ -645,13 +970,13 @@ CKB_EXPORT int ckb_topk_shard_launch(const void* x, unsigned long long* lists, v
                                      long long rows, long long cols, long long col_offset, int k, int dtype,
                                      long long chunk, cudaStream_t stream) {
   if (rows <= 0 || k <= 0) return 0;
+  if (dtype != kF32 && dtype != kBF16) return -1;
   const int elem = dtype == kBF16 ? 2 : 4;
-  if (col_offset < 0 || col_offset + cols > INT_MAX / 2 || bad_args(rows, cols, k, chunk, elem)) return -1;
+  if (col_offset < 0 || col_offset + cols > INT_MAX / 2 || bad_args(x, rows, cols, k, chunk, elem)) return -1;
   if (chunk > cols) chunk = cols;
-  ChunkArgs a{x, nullptr, nullptr, lists, (u64*)work, (unsigned*)counters, col_offset, 0, 0, k, 0, 1};
-  if (dtype == kF32) return start_chunk<float>(a, rows, cols, chunk, stream);
-  if (dtype == kBF16) return start_chunk<__nv_bfloat16>(a, rows, cols, chunk, stream);
-  return -1;
+  const SegArgs a{x, nullptr, nullptr, lists, (u64*)work, (unsigned*)counters, col_offset, (int)cols, k, 1};
+  if (dtype == kF32) return start_seg<float>(a, rows, segments(cols, chunk), stream);
+  return start_seg<__nv_bfloat16>(a, rows, segments(cols, chunk), stream);
 }
 
 // Final merge of the vocab-sharded variant (no counterpart in the reference): lists [nlists][rows][k] of sorted
@@ -661,7 +986,7 @@ CKB_EXPORT int ckb_topk_merge_launch(const unsigned long long* lists, int nlists
   if (rows <= 0 || k <= 0) return 0;
   if (nlists <= 0 || k > kMaxK || rows > INT_MAX) return -1;
   const long long smem = (long long)nlists * k * 8;
-  if (smem > kMaxDataBytes) return -1;
+  if (smem > 96 * 1024) return -1;
   if (dtype == kF32) {
     if (cudaFuncSetAttribute(topk_merge<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
@@ -680,8 +1005,9 @@ CKB_EXPORT int ckb_topk_merge_launch(const unsigned long long* lists, int nlists
   return (int)cudaGetLastError();
 }
 
-// Status of the bounded waits in this library's kernels since the last reset: 0, or 1 when a bulk-copy wait gave up.
-// Synchronises with the device; reset != 0 clears the word.
+// Status word of this library's kernels since the last reset (0 = fine). The streaming kernel waits only on its own
+// asynchronous copies, which always complete, so nothing sets it today; the entry point stays for callers that poll
+// it. Synchronises with the device; reset != 0 clears the word.
 CKB_EXPORT int ckb_topk_status(int reset) {
   unsigned v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_topk_status, sizeof(v));
@@ -700,7 +1026,7 @@ CKB_EXPORT int ckb_topk_status(int reset) {
 // GPU up front), or a latency-critical path where cudaMalloc's implicit device synchronisation is not acceptable.
 // ckb_topk_launch_noalloc serves them from a scratch array compiled into this library instead: 4 MiB of device
 // memory that every GPU which loads the library holds until the process exits. The first 256 KiB are the per-row
-// counters (up to 65536 rows), the rest the chunk workspace (491,520 composites, i.e. rows * chunks * k at most that).
+// counters (up to 65536 rows), the rest the segment workspace (491,520 composites: rows * segments * k at most that).
 constexpr size_t kNoAllocBytes = size_t(4) << 20;
 static __device__ __align__(256) unsigned long long g_noalloc_scratch[kNoAllocBytes / 8];
 
@@ -734,7 +1060,7 @@ cudaError_t noalloc_scratch(void** out) {
 // The top-k of launch() without any caller-provided workspace or counters (no counterpart in the reference): values
 // [rows, k] in x's dtype and int64 indices [rows, k] of x [rows, cols], dtype 0 (fp32) or 1 (bf16), planned as plan()
 // would with min_chunk 2048. Allocates nothing. Returns 0, -1 for arguments launch() would also reject, -2 when the
-// plan needs more than the static scratch holds (rows * chunks * k > 491,520 or rows > 65,536), or a cudaError_t.
+// plan needs more than the static scratch holds (rows * segments * k > 491,520 or rows > 65,536), or a cudaError_t.
 // The first call on a device looks up the scratch address (make it before any stream capture). Every call shares the
 // one scratch array, so calls that overlap on the GPU (different streams, no ordering between them) race; calls on
 // one stream are ordered. The counters are cleared on the caller's stream at each call.
@@ -743,21 +1069,21 @@ CKB_EXPORT int ckb_topk_launch_noalloc(const void* x, void* values, void* indice
   if (rows <= 0 || k <= 0) return 0;
   if (dtype != kF32 && dtype != kBF16) return -1;
   const int elem = dtype == kBF16 ? 2 : 4;
-  long long chunk = plan_chunk(rows, cols, elem, 2048);
-  if (bad_args(rows, cols, k, chunk, elem)) return -1;
+  long long chunk = plan_seg(rows, cols, elem, 2048);
+  if (bad_args(x, rows, cols, k, chunk, elem)) return -1;
   if (chunk > cols) chunk = cols;
-  const long long nchunks = (cols + chunk - 1) / chunk;
-  if (rows > 2 * kNoAllocCounterWords || (nchunks > 1 && rows * nchunks * k > kNoAllocWorkWords)) return -2;
+  const long long nseg = segments(cols, chunk);
+  if (rows > 2 * kNoAllocCounterWords || (nseg > 1 && rows * nseg * k > kNoAllocWorkWords)) return -2;
   void* base = nullptr;
   cudaError_t e = noalloc_scratch(&base);
   if (e != cudaSuccess) return (int)e;
   unsigned* counters = reinterpret_cast<unsigned*>(base);
   u64* work = reinterpret_cast<u64*>(base) + kNoAllocCounterWords;
-  if (nchunks > 1) {
+  if (nseg > 1) {
     e = cudaMemsetAsync(counters, 0, (size_t)rows * sizeof(unsigned), stream);
     if (e != cudaSuccess) return (int)e;
   }
-  ChunkArgs a{x, values, (long long*)indices, nullptr, work, counters, 0, 0, 0, k, 0, 0};
-  if (dtype == kF32) return start_chunk<float>(a, rows, cols, chunk, stream);
-  return start_chunk<__nv_bfloat16>(a, rows, cols, chunk, stream);
+  const SegArgs a{x, values, (long long*)indices, nullptr, work, counters, 0, (int)cols, k, 0};
+  if (dtype == kF32) return start_seg<float>(a, rows, nseg, stream);
+  return start_seg<__nv_bfloat16>(a, rows, nseg, stream);
 }

@@ -69,17 +69,22 @@ def test_rejected_arguments_return_minus_one():
     assert tk.launch(*([None] * 5), 4, 1000, 50, 0, 300, 4, 1000, None) == -1  # threads
     assert tk.launch(*([None] * 5), 4, 1000, 50, 0, 256, 3, 1000, None) == -1  # depth
     assert tk.launch(*([None] * 5), 4, 100000, 50, 0, 256, 4, 0, None) == -1  # chunk
-    assert tk.launch(*([None] * 5), 4, 100000, 50, 0, 256, 4, 100000, None) == -1  # chunk too big to stage
+    assert tk.launch(*([None] * 5), 4, 100000, 50, 0, 256, 4, 10, None) == -1  # segments * k beyond the merge
     assert tk.ckb_topk_merge_launch(None, 0, None, None, 4, 50, 0, None) == -1  # no lists
 
 
 def test_topk_plan_host_logic():
-    """plan() needs no GPU: chunks are multiples of 16 columns and fit the shared-memory staging."""
+    """plan() needs no GPU: a row splits into at most 8 segments (so any k <= 512 fits the last CTA's merge), each at
+    least min_chunk columns. The headline batch (512 rows, fewer than the 592 CTAs of 256 threads that 148 SMs hold
+    at once) streams one CTA per row in a single wave; a small batch splits its rows to fill the GPU."""
     tk = _native.load("topk")
     for rows, cols, dt in ((512, 151936, 0), (64, 151936, 0), (1, 128256, 0), (512, 32000, 1), (3, 50, 0)):
         chunk = tk.plan(rows, cols, dt, 256, 4, 2048)
-        nch = -(-cols // chunk)
+        nseg = -(-cols // chunk)
         assert 1 <= chunk <= cols
-        if nch > 1:
-            assert chunk % 16 == 0
-            assert chunk * (2 if dt else 4) <= 96 * 1024  # a chunk fits the shared-memory staging
+        assert nseg <= 8
+        if nseg > 1:
+            assert chunk >= 2048
+    assert tk.plan(512, 151936, 0, 256, 4, 2048) == 151936
+    assert -(-151936 // tk.plan(64, 151936, 0, 256, 4, 2048)) > 1
+    assert tk.plan(3, 50, 0, 256, 4, 2048) == 50

@@ -80,6 +80,49 @@ def test_misaligned_and_odd_cols_use_scalar_staging():
     _check(x, 50, vv, ii, "misaligned")
 
 
+def _launch_with_chunk(x, k, chunk):
+    lib = topk._native.load("topk")
+    rows, cols = x.shape
+    nseg = -(-cols // chunk)
+    work = torch.empty(max(1, rows * nseg * k), dtype=torch.int64, device=x.device)
+    counters = torch.zeros(rows, dtype=torch.int32, device=x.device)
+    v = torch.empty(rows, k, dtype=x.dtype, device=x.device)
+    i = torch.empty(rows, k, dtype=torch.int64, device=x.device)
+    dt = 0 if x.dtype == torch.float32 else 1
+    assert lib.launch(x.data_ptr(), v.data_ptr(), i.data_ptr(), work.data_ptr(), counters.data_ptr(), rows, cols, k,
+                      dt, 256, 4, chunk, torch.cuda.current_stream().cuda_stream) == 0
+    return v, i, counters
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("k", [50, 512])
+def test_every_segment_count(dtype, k):
+    """Rows split into 1..12 segments (odd counts pass a list through a merge round unpaired) give the same answer,
+    and every split leaves the row counters at zero."""
+    g = torch.Generator().manual_seed(k)
+    x = (torch.randn(3, 100003, generator=g) * 3).to(dtype)
+    xd = x.cuda()
+    for nseg in range(1, 13):
+        chunk = -(-x.shape[1] // nseg)
+        v, i, counters = _launch_with_chunk(xd, k, chunk)
+        _check(x, k, v, i, f"{nseg} segments")
+        assert int(counters.abs().sum()) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_increasing_rows_overflow_every_tile(dtype):
+    """Rising values: every tile beats the running top k with all of its elements, so every tile overflows the
+    candidate buffer and takes the radix-select path; falling values never get past the first tile's bound."""
+    cols = 200000 if dtype == torch.float32 else 100000
+    up = torch.arange(cols, dtype=torch.float32)
+    if dtype == torch.bfloat16:
+        up = up / 64.0  # many exact ties in bf16
+    x = torch.stack([up, up.flip(0), -up]).to(dtype)
+    for k in (50, 512):
+        vv, ii = topk.topk(x.cuda(), k)
+        _check(x, k, vv, ii, f"monotone k={k}")
+
+
 def test_repeated_calls_reuse_workspace_and_counters():
     x = workloads.topk_512x151936(scale=8)["x"].cuda()
     first = topk.topk(x, 50)

@@ -46,11 +46,12 @@ def test_matches_launch_on_two_calls_in_a_row(dtype, scale):
 
 
 def test_rejects_plans_beyond_the_scratch():
-    """512 rows x 1M columns split into tens of chunks per row: 512 * chunks * 50 composites of workspace, more than
-    the scratch holds (launch() with a caller's workspace serves it). Real buffers are passed so that even a planner
-    change could not make the call touch memory it does not own."""
+    """600 rows x 1M columns with k = 512: more rows than one wave of CTAs holds, so the plan splits each row into
+    several segments, and 600 * segments * 512 composites of workspace is more than the scratch holds (launch() with a
+    caller's workspace serves it). Real buffers are passed so that even a planner change could not make the call touch
+    memory it does not own."""
     fn = _noalloc()
-    rows, cols, k = 512, 1 << 20, 50
+    rows, cols, k = 600, 1 << 20, 512
     x = torch.empty(rows, cols, device="cuda")
     v = torch.empty(rows, k, device="cuda")
     i = torch.empty(rows, k, dtype=torch.int64, device="cuda")
