@@ -49,35 +49,40 @@ typedef unsigned long long u64;
 #define CKB_TOPK_UNROLL 4
 #endif
 #ifndef CKB_TOPK_STAGES_256
-#define CKB_TOPK_STAGES_256 4
+#define CKB_TOPK_STAGES_256 3
 #endif
 #ifndef CKB_TOPK_UNROLL_256
-#define CKB_TOPK_UNROLL_256 2
+#define CKB_TOPK_UNROLL_256 4
+#endif
+#ifndef CKB_TOPK_SLOTS_256
+#define CKB_TOPK_SLOTS_256 10
 #endif
 #ifndef CKB_TOPK_WIDE_ONLY
 #define CKB_TOPK_WIDE_ONLY 0
 #endif
-constexpr int kCand = 1024;                       // running top k + survivors since the last compaction
-constexpr int kPack = 512;                        // compaction scratch: select output, packing, 1024-bin histogram
+#ifndef CKB_TOPK_SPEC_Z
+#define CKB_TOPK_SPEC_Z 4.5f
+#endif
 #ifndef CKB_TOPK_SPEC_MARGIN
-#define CKB_TOPK_SPEC_MARGIN 12
+#define CKB_TOPK_SPEC_MARGIN 3.0f
 #endif
-#ifndef CKB_TOPK_SPEC_SCALE
-#define CKB_TOPK_SPEC_SCALE 1.0f
-#endif
-// Speculative bound after a compaction: the m-th largest composite seen, m = ceil(scale * k * fraction seen) + margin.
-// With i.i.d. values the segment's count above it is about m / fraction seen; falling short of k needs a Gamma(m)
-// variable below k * fraction, which the margin makes rare (and the kernel checks for it anyway).
-constexpr int kSpecMargin = CKB_TOPK_SPEC_MARGIN;
-constexpr float kSpecScale = CKB_TOPK_SPEC_SCALE;
+// Speculative bound after a compaction: the m-th largest composite seen so far. The bound is too high only when the
+// seen part (a fraction f of the segment) holds m or more of the segment's top k elements; with values in random
+// order that count is about Poisson(k f), so m = ceil(k f + z sqrt(k f) + margin) makes a miss rare (the kernel
+// checks for it and then streams the segment again with guaranteed bounds).
+constexpr float kSpecZ = CKB_TOPK_SPEC_Z;
+constexpr float kSpecMargin = CKB_TOPK_SPEC_MARGIN;
+__device__ __forceinline__ int spec_rank(int k, float seen) {
+  const float kf = (float)k * seen;
+  return (int)ceilf(kf + kSpecZ * sqrtf(kf) + kSpecMargin);
+}
 constexpr int kMaxK = 512;
 constexpr int kDirectSelect = 192;                // compactions of more candidates narrow them by radix first
-constexpr int kRadixBins = 1024;                  // 10-bit digits
-constexpr int kLevels = 7;                        // 6 x 10 bits + 4 bits cover the 64-bit composite
-constexpr int kSlots = 12;                        // survivor vectors a warp records between compactions
-constexpr int kSlotsFull = 8;                     // a warp holding this many asks for a compaction
 constexpr int kSmPerSmBytes = 233472;             // shared memory per SM (228 KB)
 
+// Per shape: the ring, the candidate buffer (the running top k and the survivors behind it, so at least 2 kMaxK), the
+// compaction scratch (select output, packing, or the radix histogram of kDigit-bit digits) and the warps' survivor
+// slots. The 256-thread shape keeps all of it within a quarter of an SM's shared memory.
 template <int NT>
 struct Cfg {
   static constexpr int kWarps = NT / 32;
@@ -86,28 +91,38 @@ struct Cfg {
   static constexpr int kU = NT == 512 ? CKB_TOPK_UNROLL : CKB_TOPK_UNROLL_256;      // vectors per thread per tile
   static constexpr int kTileVecs = NT * kU;       // thread t holds vectors u * NT + t of a tile
   static constexpr int kRingBytes = kStages * kTileVecs * 16;
+  static constexpr int kCand = 2 * kMaxK;         // running top k + survivors since the last compaction
+  static constexpr int kPack = kMaxK;             // compaction scratch entries
+  static constexpr int kDigit = NT == 512 ? 10 : 9;
+  static constexpr int kRadixBins = 1 << kDigit;
+  static constexpr int kLevels = (64 + kDigit - 1) / kDigit;
+  static constexpr int kSlots = NT == 512 ? 12 : CKB_TOPK_SLOTS_256;  // vectors a warp records between compactions
+  static constexpr int kSlotsFull = kSlots - 4;       // a warp holding this many asks for a compaction
   static constexpr int kSlotBytes = kWarps * kSlots * 20;  // recorded vectors (16 bytes) and indices (4 bytes)
   static constexpr int kSmemBytes = kRingBytes + kCand * 8 + kPack * 8 + kSlotBytes;
   static constexpr int kMergeEntries = kRingBytes / 16;    // nseg * k: the merge ping-pongs between ring halves
   static constexpr int kMinBlocks = NT == 512 ? 2 : 4;
+  // Each CTA also holds 1 KB the hardware reserves and a few hundred bytes of static shared memory.
   static constexpr int kCtasPerSm =
-      kSmPerSmBytes / (kSmemBytes + 2048) < kMinBlocks ? kSmPerSmBytes / (kSmemBytes + 2048) : kMinBlocks;
+      kSmPerSmBytes / (kSmemBytes + 1280) < kMinBlocks ? kSmPerSmBytes / (kSmemBytes + 1280) : kMinBlocks;
   static_assert(kMaxK <= 32 * kWarps, "the first tile's bound needs ceil(k / warps) <= 32");
   static_assert(kCand - kMaxK >= kMaxK, "after a compaction a radix select must leave room for k survivors");
   static_assert(kMergeEntries >= kMaxK, "the ring must hold one list per segment");
   static_assert(kRadixBins % NT == 0, "histogram bins split evenly over the threads");
+  static_assert(kRadixBins * 4 <= kPack * 8, "the radix histogram lives in the compaction scratch");
+  static_assert(kSlots <= 32, "a warp expands its slots one per lane");
   static_assert(kCtasPerSm >= 1, "one CTA's shared memory fits an SM");
 };
 // Segments per row that every k fits in either shape's merge.
 constexpr int kMaxSeg = Cfg<256>::kMergeEntries / Cfg<256>::kMaxK < Cfg<512>::kMergeEntries / Cfg<512>::kMaxK
                             ? Cfg<256>::kMergeEntries / Cfg<256>::kMaxK
                             : Cfg<512>::kMergeEntries / Cfg<512>::kMaxK;
-static_assert(kRadixBins * 4 <= kPack * 8, "the radix histogram lives in the compaction scratch");
-static_assert(kSlots <= 32, "a warp expands its slots one per lane");
 
-// Radix digits over the 64-bit composite, most significant first: six of 10 bits, then the last 4.
-__device__ __forceinline__ int level_shift(int L) { return L < 6 ? 54 - 10 * L : 0; }
-__device__ __forceinline__ int level_width(int L) { return L < 6 ? 10 : 4; }
+// Radix digits of D bits over the 64-bit composite, most significant first (the last digit takes what is left).
+template <int D>
+__device__ __forceinline__ int level_shift(int L) { return 64 - D * (L + 1) > 0 ? 64 - D * (L + 1) : 0; }
+template <int D>
+__device__ __forceinline__ int level_width(int L) { return 64 - D * L < D ? 64 - D * L : D; }
 
 __device__ __forceinline__ unsigned order_key(unsigned bits) {
   return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
@@ -316,11 +331,12 @@ __device__ __forceinline__ void for_each_at_least(const TileRegs<T, NT, U>& t, u
   }
 }
 
-// Appends the tile's composites >= lo to buf[off + ...] (entries past kCand are dropped; *counter counts them all).
+// Appends the tile's composites >= lo to buf[off + ...] (entries past cap are dropped; *counter counts them all).
 // A float compare per vector finds the few that may qualify; only those build their composites, and a warp that has
 // any reserves its slots with one shared atomic. Every lane of every warp calls it.
 template <typename T, int NT, int U>
 __device__ __forceinline__ void collect(const TileRegs<T, NT, U>& t, u64 lo, u64* buf, int off, int* counter) {
+  constexpr int cap = Cfg<NT>::kCand;
   constexpr int V = VecN<T>::N;
   const T* tag = nullptr;
   const float f_lo = __uint_as_float(key_bits((unsigned)(lo >> 32)));
@@ -339,22 +355,23 @@ __device__ __forceinline__ void collect(const TileRegs<T, NT, U>& t, u64 lo, u64
     int pos = off + warp_reserve(__popc(take), counter);
     for (; take; take &= take - 1u, ++pos) {
       const int e = __ffs(take) - 1;
-      if (pos < kCand) buf[pos] = composite(order_key(elem_bits(t.r[u], e, tag)), idx0 + (unsigned)e);
+      if (pos < cap) buf[pos] = composite(order_key(elem_bits(t.r[u], e, tag)), idx0 + (unsigned)e);
     }
   }
   if (__any_sync(0xffffffffu, t.has_x)) {
     const u64 c = composite(order_key(t.xbits), t.xidx);
     const bool keep = t.has_x && c >= lo;
     const int pos = off + warp_reserve(keep ? 1 : 0, counter);
-    if (keep && pos < kCand) buf[pos] = c;
+    if (keep && pos < cap) buf[pos] = c;
   }
 }
 
 // Records, for tiles after the first, each of this thread's vectors that may hold a composite >= lo (its largest value
 // not below f_lo, NaN included) in its warp's slots: the vector and its index within the segment, at a place found
 // by a ballot (no atomics, no composites; those are built when the slots are expanded). Returns the warp's new count;
-// slots past kSlots are not written (the caller sees the count exceed kSlots). Every lane of the warp calls it.
-template <typename T, int NT, int U>
+// slots past the shape's kSlots are not written (the caller sees the count exceed them). Every lane of the warp calls
+// it.
+template <bool kFull, typename T, int NT, int U>
 __device__ __forceinline__ int record(const TileRegs<T, NT, U>& t, float f_lo, uint4* wslot, unsigned* widx,
                                       int wcnt) {
   const T* tag = nullptr;
@@ -362,12 +379,12 @@ __device__ __forceinline__ int record(const TileRegs<T, NT, U>& t, float f_lo, u
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const int v = t.vb + u * NT;
-    const bool maybe = v < t.nv && !(vec_max_nan(t.r[u], tag) < f_lo);
+    const bool maybe = (kFull || v < t.nv) && !(vec_max_nan(t.r[u], tag) < f_lo);
     const unsigned bal = __ballot_sync(0xffffffffu, maybe);
     if (bal == 0u) continue;
     if (maybe) {
       const int pos = wcnt + __popc(bal & below);
-      if (pos < kSlots) {
+      if (pos < Cfg<NT>::kSlots) {
         wslot[pos] = t.r[u];
         widx[pos] = (unsigned)v;
       }
@@ -378,9 +395,9 @@ __device__ __forceinline__ int record(const TileRegs<T, NT, U>& t, float f_lo, u
 }
 
 // Appends the composites >= lo of this warp's n recorded vectors (n <= kSlots, one per lane) to buf[off + ...]
-// (entries past kCand are dropped; *counter counts them all); with buf null it only counts them. Every lane of the
+// (entries past cap are dropped; *counter counts them all); with buf null it only counts them. Every lane of the
 // warp calls it.
-template <typename T>
+template <typename T, int cap>
 __device__ __forceinline__ void expand(const uint4* wslot, const unsigned* widx, int n, unsigned base_idx, u64 lo,
                                        u64* buf, int off, int* counter) {
   constexpr int V = VecN<T>::N;
@@ -403,7 +420,7 @@ __device__ __forceinline__ void expand(const uint4* wslot, const unsigned* widx,
   int pos = off + warp_reserve(__popc(take), counter);
   for (; take; take &= take - 1u, ++pos) {
     const int e = __ffs(take) - 1;
-    if (pos < kCand) buf[pos] = composite(order_key(elem_bits(r, e, tag)), idx0 + (unsigned)e);
+    if (pos < cap) buf[pos] = composite(order_key(elem_bits(r, e, tag)), idx0 + (unsigned)e);
   }
 }
 
@@ -427,16 +444,17 @@ __device__ __forceinline__ void for_each_recorded(const uint4* wslot, const unsi
 // Radix select: the lower edge of the digit bin holding the kk-th largest of the items that each thread's
 // items(f) visits, refined digit by digit (10 bits at a time from the top of the composite, so value ties resolve by
 // index) until the items >= edge number at most cap (cap >= kk: the last digit leaves exactly kk). Every level
-// rebuilds the histogram `hist` (kRadixBins words). All threads call it; it ends with a barrier.
+// rebuilds the histogram `hist` (the shape's kRadixBins words). All threads call it; it ends with a barrier.
 template <int NT, typename Items>
 __device__ u64 radix_edge(Items&& items, unsigned kk, int cap, unsigned* hist, unsigned* warp_tot, int* s_bin,
                           unsigned* s_above) {
   u64 prefix = 0, edge = 0;
   unsigned above_total = 0;
-  for (int L = 0; L < kLevels; ++L) {
-    const int sh = level_shift(L), w = level_width(L);
+  using C = Cfg<NT>;
+  for (int L = 0; L < C::kLevels; ++L) {
+    const int sh = level_shift<C::kDigit>(L), w = level_width<C::kDigit>(L);
     const unsigned mask = (1u << w) - 1u;
-    for (int i = threadIdx.x; i < kRadixBins; i += NT) hist[i] = 0u;
+    for (int i = threadIdx.x; i < C::kRadixBins; i += NT) hist[i] = 0u;
     if (threadIdx.x == 0) *s_bin = 0;
     __syncthreads();
     items([&](u64 c) {
@@ -448,7 +466,7 @@ __device__ u64 radix_edge(Items&& items, unsigned kk, int cap, unsigned* hist, u
     const unsigned above = *s_above, inbin = hist[bin];
     const u64 next = (prefix << w) | (u64)bin;
     edge = next << sh;
-    if (above_total + above + inbin <= (unsigned)cap || L == kLevels - 1) break;
+    if (above_total + above + inbin <= (unsigned)cap || L == C::kLevels - 1) break;
     above_total += above;
     kk -= above;
     prefix = next;
@@ -489,6 +507,7 @@ __device__ __forceinline__ void select_top(const u64* cand, int cnt, int k, u64*
 template <int NT>
 __device__ int compact(u64* cand, int n, int k, u64* tmp, unsigned* warp_tot, int* s_bin, unsigned* s_above,
                        int* s_pack) {
+  constexpr int kPack = Cfg<NT>::kPack;
   const int cap = min(kPack, max(kDirectSelect, k + 32));
   if (n <= cap) {
     select_top<NT>(cand, n, k, tmp);
@@ -552,6 +571,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   constexpr int V = VecN<T>::N;
   constexpr int kThreads = NT, kWarps = C::kWarps, kU = C::kU, kStages = C::kStages, kTileVecs = C::kTileVecs;
   constexpr int kRingBytes = C::kRingBytes, kMergeEntries = C::kMergeEntries;
+  constexpr int kCand = C::kCand, kPack = C::kPack, kSlots = C::kSlots, kSlotsFull = C::kSlotsFull;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ unsigned warp_tot[kWarps];
   __shared__ unsigned warp_key[kWarps];
@@ -600,24 +620,47 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   }
 
   const int ntiles = max(1, (nv + kTileVecs - 1) / kTileVecs);
-  // Tile j's vectors of this thread into stage j % kStages; one commit group per tile (empty past the last tile).
-  auto issue = [&](int j) {
+  const int full_tiles = nv / kTileVecs;  // tiles whose every vector lies in the segment
+  // Tile j's vectors of this thread into ring stage `stage`; one commit group per tile (empty past the last tile).
+  auto issue = [&](int j, int stage) {
     if (j < ntiles) {
-      uint4* st = ring + (j % kStages) * kTileVecs;
+      const uint4* src = body + j * kTileVecs + tid;
+      uint4* dst = ring + stage * kTileVecs + tid;
+      if (j < full_tiles) {
 #pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int v = j * kTileVecs + u * kThreads + tid;
-        if (v < nv) cp_async16(st + u * kThreads + tid, body + v);
+        for (int u = 0; u < kU; ++u) cp_async16(dst + u * kThreads, src + u * kThreads);
+      } else {
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+          if (j * kTileVecs + u * kThreads + tid < nv) cp_async16(dst + u * kThreads, src + u * kThreads);
       }
     }
     cp_async_commit();
+  };
+  // This thread's vectors of tile j (landed in ring stage `stage`) into t; vectors past the segment read as NaN.
+  auto load = [&](int j, int stage) {
+    const uint4* st = ring + stage * kTileVecs + tid;
+    t.vb = j * kTileVecs + tid;
+    if (j < full_tiles) {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) t.r[u] = st[u * kThreads];
+    } else {
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        t.r[u] = t.vb + u * kThreads < nv ? st[u * kThreads]
+                                           : make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
+    }
+  };
+  // The fraction of the segment in tiles 0..j.
+  const float seg_elems = (float)nv * V + (float)nextra;
+  auto seen_after = [&](int j) {
+    return ((float)min(nv, (j + 1) * kTileVecs) * V + (float)nextra) / seg_elems;
   };
 
   // Pass 0 speculates: the bound rises to the m-th largest composite seen so far (m sized so that the whole segment
   // almost surely holds k composites above it). The answer is exact when the final k-th composite reaches every
   // speculative bound used (then no element left out can rank in the top k); otherwise pass 1 streams the segment
   // again with guaranteed bounds only.
-  const float seg_elems = (float)nv * V + (float)nextra;
   int ntop = 0;    // entries of the running top in cand[0, ntop), sorted
   int filled = 0;  // survivors appended behind it since the last compaction
   u64 lo = 0;      // every composite that can still enter the top k (or, speculating, pass the check) is >= lo
@@ -637,7 +680,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
     if (ntop == k) {
       lo = raise_bound(lo, cand[k - 1]);
       if (speculate && seen >= 0.0f) {
-        const int m = (int)ceilf(kSpecScale * (float)k * seen) + kSpecMargin;
+        const int m = spec_rank(k, seen);
         if (m < k) {
           const u64 s_m = cand[m - 1];
           spec = s_m > spec ? s_m : spec;
@@ -675,14 +718,14 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
     if (ntop + filled + kWarps * kSlots * V <= kCand) {  // every composite of every slot fits: no count needed
       if (tid == 0) s_cnt = 0;
       __syncthreads();
-      expand<T>(wslot, widx, n, t.base_idx, lo, cand, ntop + filled, &s_cnt);
+      expand<T, kCand>(wslot, widx, n, t.base_idx, lo, cand, ntop + filled, &s_cnt);
       __syncthreads();
       take_count();
       return;
     }
     if (tid == 0) s_cnt = 0;
     __syncthreads();
-    expand<T>(wslot, widx, n, t.base_idx, lo, nullptr, 0, &s_cnt);
+    expand<T, kCand>(wslot, widx, n, t.base_idx, lo, nullptr, 0, &s_cnt);
     __syncthreads();
     const int need = s_cnt;
     __syncthreads();
@@ -696,7 +739,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
     }
     if (tid == 0) s_cnt = 0;
     __syncthreads();
-    expand<T>(wslot, widx, n, t.base_idx, lo, cand, ntop + filled, &s_cnt);
+    expand<T, kCand>(wslot, widx, n, t.base_idx, lo, cand, ntop + filled, &s_cnt);
     __syncthreads();
     take_count();
   };
@@ -704,74 +747,80 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   for (int pass = 0; pass < 2; ++pass) {
     speculate = pass == 0;
 #pragma unroll
-    for (int j = 0; j < kStages - 1; ++j) issue(j);
+    for (int j = 0; j < kStages - 1; ++j) issue(j, j);
     for (int i = tid; i < k; i += kThreads) cand[i] = 0ull;
     if (tid < 3) s_flag[tid] = 0;
     ntop = 0;
     filled = 0;
     lo = 0;
     spec = 0;
-    int wcnt = 0;  // this warp's recorded vectors
-    for (int j = 0; j < ntiles; ++j) {
-      issue(j + kStages - 1);
-      cp_async_wait<kStages - 1>();  // this thread's copies of tile j have landed
-      const uint4* st = ring + (j % kStages) * kTileVecs + tid;
-      t.vb = j * kTileVecs + tid;
-#pragma unroll
-      for (int u = 0; u < kU; ++u)
-        t.r[u] = t.vb + u * kThreads < nv ? st[u * kThreads]
-                                           : make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
-      t.has_x = j == 0 && mine_x;
-      const float seen = ((float)min(nv, (j + 1) * kTileVecs) * V + (float)nextra) / seg_elems;
 
-      if (j == 0) {
-        // The bound: c-th largest per-thread maximum of each warp (key 0 when a thread saw no number), smallest over
-        // the warps. Key 0 is no number's key, so a warp short of c numbers leaves the bound at 0: no bound.
-        float fm = __int_as_float(0x7fc00000);
+    // Tile 0: the bound, every composite at or above it, and a first compaction that sets the running bounds.
+    issue(kStages - 1, kStages - 1);
+    cp_async_wait<kStages - 1>();
+    load(0, 0);
+    t.has_x = mine_x;
+    {
+      // The c-th largest per-thread maximum of each warp (key 0 when a thread saw no number), smallest over the
+      // warps. Key 0 is no number's key, so a warp short of c numbers leaves the bound at 0: no bound.
+      float fm = __int_as_float(0x7fc00000);
 #pragma unroll
-        for (int u = 0; u < kU; ++u) fm = vec_max(t.r[u], fm, tag);
-        if (t.has_x) fm = max3(fm, __uint_as_float(t.xbits), __uint_as_float(t.xbits));
-        // A bitonic sort of the 32 keys across the lanes, descending: lane l ends with the (l + 1)-th largest.
-        unsigned key = fm == fm ? order_key(__float_as_uint(fm)) : 0u;
+      for (int u = 0; u < kU; ++u) fm = vec_max(t.r[u], fm, tag);
+      if (t.has_x) fm = max3(fm, __uint_as_float(t.xbits), __uint_as_float(t.xbits));
+      // A bitonic sort of the 32 keys across the lanes, descending: lane l ends with the (l + 1)-th largest.
+      unsigned key = fm == fm ? order_key(__float_as_uint(fm)) : 0u;
 #pragma unroll
-        for (int size = 2; size <= 32; size <<= 1) {
+      for (int size = 2; size <= 32; size <<= 1) {
 #pragma unroll
-          for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            const unsigned o = __shfl_xor_sync(0xffffffffu, key, stride);
-            const bool keep_max = ((lane & stride) == 0) == ((lane & size) == 0);
-            key = keep_max ? max(key, o) : min(key, o);
-          }
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          const unsigned o = __shfl_xor_sync(0xffffffffu, key, stride);
+          const bool keep_max = ((lane & stride) == 0) == ((lane & size) == 0);
+          key = keep_max ? max(key, o) : min(key, o);
         }
-        const unsigned wk = __shfl_sync(0xffffffffu, key, (k + kWarps - 1) / kWarps - 1);
-        if (lane == 0) warp_key[warp] = wk;
-        __syncthreads();
-        unsigned b = warp_key[0];
-#pragma unroll
-        for (int w = 1; w < kWarps; ++w) b = min(b, warp_key[w]);
-        lo = (u64)b << 32;
-        collect_tile();
-        compact_all(seen);
-        continue;
       }
-
-      // Later tiles: record the vectors that may hold a survivor; expand and compact only when a warp's slots fill.
-      const int before = wcnt;
-      wcnt = record(t, __uint_as_float(key_bits((unsigned)(lo >> 32))), wslot, widx, wcnt);
-      if (lane == 0 && wcnt >= kSlotsFull) atomicOr(&s_flag[j % 3], wcnt > kSlots ? 3 : 1);
-      if (tid == 0) s_flag[(j + 1) % 3] = 0;  // its last reads came before the barrier of tile j - 1
+      const unsigned wk = __shfl_sync(0xffffffffu, key, (k + kWarps - 1) / kWarps - 1);
+      if (lane == 0) warp_key[warp] = wk;
       __syncthreads();
-      const int flag = s_flag[j % 3];
+      unsigned b = warp_key[0];
+#pragma unroll
+      for (int w = 1; w < kWarps; ++w) b = min(b, warp_key[w]);
+      lo = (u64)b << 32;
+    }
+    collect_tile();
+    compact_all(seen_after(0));
+    t.has_x = false;
+
+    // Later tiles: record the vectors that may hold a survivor; expand and compact only when a warp's slots fill.
+    int wcnt = 0;                           // this warp's recorded vectors
+    int rs = kStages > 1 ? 1 % kStages : 0;  // ring stage of tile j
+    int fs = 1;                             // s_flag word of tile j
+    float f_lo = __uint_as_float(key_bits((unsigned)(lo >> 32)));
+    for (int j = 1; j < ntiles; ++j) {
+      issue(j + kStages - 1, rs == 0 ? kStages - 1 : rs - 1);  // into the stage tile j - 1 left
+      cp_async_wait<kStages - 1>();                            // this thread's copies of tile j have landed
+      load(j, rs);
+      const int before = wcnt;
+      wcnt = j < full_tiles ? record<true>(t, f_lo, wslot, widx, wcnt) : record<false>(t, f_lo, wslot, widx, wcnt);
+      if (lane == 0 && wcnt >= kSlotsFull) atomicOr(&s_flag[fs], wcnt > kSlots ? 3 : 1);
+      const int fnext = fs == 2 ? 0 : fs + 1;
+      if (tid == 0) s_flag[fnext] = 0;  // its last reads came before the barrier of tile j - 1
+      __syncthreads();
+      const int flag = s_flag[fs];
       if (flag & 2) {
         // Some warp overflowed: keep every warp's records from earlier tiles, take this tile from registers.
         expand_all(before);
         wcnt = 0;
         collect_tile();
-        compact_all(seen);
+        compact_all(seen_after(j));
+        f_lo = __uint_as_float(key_bits((unsigned)(lo >> 32)));
       } else if (flag & 1) {
         expand_all(wcnt);
         wcnt = 0;
-        if (filled > 0) compact_all(seen);
+        if (filled > 0) compact_all(seen_after(j));
+        f_lo = __uint_as_float(key_bits((unsigned)(lo >> 32)));
       }
+      rs = rs + 1 == kStages ? 0 : rs + 1;
+      fs = fnext;
     }
     expand_all(wcnt);
     if (filled > 0) ntop = compact<NT>(cand, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
@@ -848,43 +897,28 @@ __global__ void __launch_bounds__(256) topk_merge(const u64* __restrict__ lists,
   }
 }
 
-// The CTA shape for k: 256 threads whenever k fits that shape's bound, else 512.
-inline bool narrow_for(int k) { return !CKB_TOPK_WIDE_ONLY && k <= Cfg<256>::kMaxK; }
-constexpr int kPlanShape = CKB_TOPK_WIDE_ONLY ? 512 : 256;  // the shape plan() assumes (k <= 256)
+// The CTA shape. 256 threads (4 CTAs per SM) when k fits its bound and the batch has at least two rows per SM:
+// every row streams in its own CTA, all in one wave. Smaller batches (and k > 256) take 512 threads (2 per SM), the
+// deeper ring per CTA, and split rows to fill the GPU.
+inline bool narrow_for(long long rows, int k) {
+  return !CKB_TOPK_WIDE_ONLY && k <= Cfg<256>::kMaxK && rows >= 2LL * device_sm_count();
+}
 
-// Segments per row: the count (1 .. kMaxSeg, each at least min_chunk columns) with the least modelled time. CTAs run
-// in waves of kCtasPerSm per SM; while the GPU is full each CTA streams at the HBM bandwidth's share of one slot,
-// otherwise at what its own ring keeps in flight (kStages - 1 tiles per load latency). A CTA also pays a fixed start
-// (first tile's latency, the bound) and a split row one merge round per halving of its lists.
-constexpr double kHbmBytesPerNs = 6500.0;
-constexpr double kLoadLatencyNs = 1500.0;
-constexpr double kCtaFixedNs = 600.0;
-constexpr double kMergeRoundNs = 300.0;
-
+// Segments per row (each at least min_chunk columns, at most kMaxSeg): one row per CTA once the batch fills the GPU,
+// otherwise about one CTA per SM in all (measured on B200: more CTAs of the 512-thread shape gain nothing, and each
+// split adds a merge).
 long long plan_seg(long long rows, long long cols, int elem, int min_chunk) {
-  using C = Cfg<kPlanShape>;
+  (void)elem;
   if (rows <= 0 || cols <= 0) return cols > 0 ? cols : 1;
   if (min_chunk < 1024) min_chunk = 1024;
-  const long long slots = (long long)device_sm_count() * C::kCtasPerSm;
-  const double cta_bw = (double)(C::kStages - 1) * C::kTileVecs * 16 / kLoadLatencyNs;
-  long long best_n = 1;
-  double best = 0.0;
-  for (long long n = 1; n <= kMaxSeg; ++n) {
-    if (n > 1 && cols / n < min_chunk) break;
-    const long long ctas = rows * n;
-    const long long active = ctas < slots ? ctas : slots;
-    double bw = kHbmBytesPerNs / (double)active;
-    if (bw > cta_bw) bw = cta_bw;
-    const long long waves = (ctas + slots - 1) / slots;
-    int rounds = 0;
-    for (long long m = n; m > 1; m = (m + 1) / 2) ++rounds;
-    const double ns = (double)waves * ((double)cols * elem / (double)n / bw + kCtaFixedNs) + rounds * kMergeRoundNs;
-    if (n == 1 || ns < best) {
-      best = ns;
-      best_n = n;
-    }
+  long long n = 1;
+  if (rows < 2LL * device_sm_count()) {
+    n = device_sm_count() / rows;
+    if (n > kMaxSeg) n = kMaxSeg;
+    if (n > cols / min_chunk) n = cols / min_chunk;
+    if (n < 1) n = 1;
   }
-  return (cols + best_n - 1) / best_n;
+  return (cols + n - 1) / n;
 }
 
 // Sets the kernel's shared-memory limit once per device.
@@ -915,7 +949,7 @@ int start_shape(const SegArgs& a, long long rows, long long nseg, cudaStream_t s
 
 template <typename T>
 int start_seg(const SegArgs& a, long long rows, long long nseg, cudaStream_t s) {
-  return narrow_for(a.k) ? start_shape<T, 256>(a, rows, nseg, s) : start_shape<T, 512>(a, rows, nseg, s);
+  return narrow_for(rows, a.k) ? start_shape<T, 256>(a, rows, nseg, s) : start_shape<T, 512>(a, rows, nseg, s);
 }
 
 long long segments(long long cols, long long chunk) { return (cols + chunk - 1) / chunk; }
@@ -926,7 +960,7 @@ bool bad_args(const void* x, long long rows, long long cols, int k, long long ch
   if (k > cols || k > kMaxK || cols > INT_MAX / 2 || rows > 65535 || chunk <= 0) return true;
   if (reinterpret_cast<uintptr_t>(x) % (uintptr_t)elem) return true;
   if (chunk > cols) chunk = cols;
-  const long long cap = narrow_for(k) ? Cfg<256>::kMergeEntries : Cfg<512>::kMergeEntries;
+  const long long cap = narrow_for(rows, k) ? Cfg<256>::kMergeEntries : Cfg<512>::kMergeEntries;
   return segments(cols, chunk) * k > cap;
 }
 

@@ -45,20 +45,24 @@ def test_matches_launch_on_two_calls_in_a_row(dtype, scale):
         assert bits_equal(v, want_v), f"call {call}: values differ"
 
 
-def test_rejects_plans_beyond_the_scratch():
-    """600 rows x 1M columns with k = 512: more rows than one wave of CTAs holds, so the plan splits each row into
-    several segments, and 600 * segments * 512 composites of workspace is more than the scratch holds (launch() with a
-    caller's workspace serves it). Real buffers are passed so that even a planner change could not make the call touch
-    memory it does not own."""
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_split_rows_merge_through_the_scratch_call_after_call(dtype):
+    """A small batch of long rows is split into several segments per row, so the call merges through the scratch
+    workspace and its per-row counters (which must be left reusable): two calls in a row equal launch()."""
     fn = _noalloc()
-    rows, cols, k = 600, 1 << 20, 512
-    x = torch.empty(rows, cols, device="cuda")
-    v = torch.empty(rows, k, device="cuda")
-    i = torch.empty(rows, k, dtype=torch.int64, device="cuda")
+    g = torch.Generator().manual_seed(5)
+    x = (torch.randn(2, 1 << 20, generator=g) * 3).to(dtype).cuda()
     plan = ctypes.CDLL(build.lib_path("topk")).plan
     plan.restype = ctypes.c_longlong
     plan.argtypes = [ctypes.c_longlong, ctypes.c_longlong, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
-    nseg = -(-cols // plan(rows, cols, 0, 256, 4, 2048))
-    assert nseg > 1 and rows * nseg * k > 491520
-    assert fn(x.data_ptr(), v.data_ptr(), i.data_ptr(), rows, cols, k, 0, torch.cuda.current_stream().cuda_stream) == -2
-    torch.cuda.synchronize()
+    dt = 0 if dtype == torch.float32 else 1
+    assert -(-x.shape[1] // plan(2, x.shape[1], dt, 256, 4, 2048)) > 1
+    want_v, want_i = topk.topk(x, 50)
+    for call in range(2):
+        v = torch.empty(2, 50, dtype=dtype, device="cuda")
+        i = torch.empty(2, 50, dtype=torch.int64, device="cuda")
+        assert fn(x.data_ptr(), v.data_ptr(), i.data_ptr(), 2, x.shape[1], 50, dt,
+                  torch.cuda.current_stream().cuda_stream) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(i, want_i), f"call {call}: indices differ"
+        assert bits_equal(v, want_v), f"call {call}: values differ"
