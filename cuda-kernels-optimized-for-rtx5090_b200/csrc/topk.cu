@@ -57,6 +57,17 @@ typedef unsigned long long u64;
 #ifndef CKB_TOPK_SLOTS_256
 #define CKB_TOPK_SLOTS_256 10
 #endif
+// The 256-thread shape for 2-byte elements: a shallower ring with more survivor slots (a 16-byte vector holds 8
+// elements, so more vectors pass the pre-filter per survivor and expansions are costlier).
+#ifndef CKB_TOPK_STAGES_256H
+#define CKB_TOPK_STAGES_256H 2
+#endif
+#ifndef CKB_TOPK_UNROLL_256H
+#define CKB_TOPK_UNROLL_256H 4
+#endif
+#ifndef CKB_TOPK_SLOTS_256H
+#define CKB_TOPK_SLOTS_256H 32
+#endif
 #ifndef CKB_TOPK_WIDE_ONLY
 #define CKB_TOPK_WIDE_ONLY 0
 #endif
@@ -73,8 +84,8 @@ typedef unsigned long long u64;
 constexpr float kSpecZ = CKB_TOPK_SPEC_Z;
 constexpr float kSpecMargin = CKB_TOPK_SPEC_MARGIN;
 __device__ __forceinline__ int spec_rank(int k, float seen) {
-  const float kf = (float)k * seen;
-  return (int)ceilf(kf + kSpecZ * sqrtf(kf) + kSpecMargin);
+  const float kf = (float)k * fminf(fmaxf(seen, 0.0f), 1.0f);
+  return min(k, (int)ceilf(kf + kSpecZ * sqrtf(kf) + kSpecMargin));
 }
 constexpr int kMaxK = 512;
 constexpr int kDirectSelect = 192;                // compactions of more candidates narrow them by radix first
@@ -83,12 +94,14 @@ constexpr int kSmPerSmBytes = 233472;             // shared memory per SM (228 K
 // Per shape: the ring, the candidate buffer (the running top k and the survivors behind it, so at least 2 kMaxK), the
 // compaction scratch (select output, packing, or the radix histogram of kDigit-bit digits) and the warps' survivor
 // slots. The 256-thread shape keeps all of it within a quarter of an SM's shared memory.
-template <int NT>
+template <int NT, int EB = 4>  // EB: element bytes (the ring and slots differ; the rest is the same for both)
 struct Cfg {
   static constexpr int kWarps = NT / 32;
   static constexpr int kMaxK = NT == 512 ? 512 : 256;              // c = ceil(k / kWarps) <= 32
-  static constexpr int kStages = NT == 512 ? CKB_TOPK_STAGES : CKB_TOPK_STAGES_256;  // ring depth
-  static constexpr int kU = NT == 512 ? CKB_TOPK_UNROLL : CKB_TOPK_UNROLL_256;      // vectors per thread per tile
+  static constexpr int kStages =                                    // ring depth
+      NT == 512 ? CKB_TOPK_STAGES : EB == 4 ? CKB_TOPK_STAGES_256 : CKB_TOPK_STAGES_256H;
+  static constexpr int kU =                                         // vectors per thread per tile
+      NT == 512 ? CKB_TOPK_UNROLL : EB == 4 ? CKB_TOPK_UNROLL_256 : CKB_TOPK_UNROLL_256H;
   static constexpr int kTileVecs = NT * kU;       // thread t holds vectors u * NT + t of a tile
   static constexpr int kRingBytes = kStages * kTileVecs * 16;
   static constexpr int kCand = 2 * kMaxK;         // running top k + survivors since the last compaction
@@ -96,7 +109,8 @@ struct Cfg {
   static constexpr int kDigit = NT == 512 ? 10 : 9;
   static constexpr int kRadixBins = 1 << kDigit;
   static constexpr int kLevels = (64 + kDigit - 1) / kDigit;
-  static constexpr int kSlots = NT == 512 ? 12 : CKB_TOPK_SLOTS_256;  // vectors a warp records between compactions
+  static constexpr int kSlots =  // vectors a warp records between compactions
+      NT == 512 ? 12 : EB == 4 ? CKB_TOPK_SLOTS_256 : CKB_TOPK_SLOTS_256H;
   static constexpr int kSlotsFull = kSlots - 4;       // a warp holding this many asks for a compaction
   static constexpr int kSlotBytes = kWarps * kSlots * 20;  // recorded vectors (16 bytes) and indices (4 bytes)
   static constexpr int kSmemBytes = kRingBytes + kCand * 8 + kPack * 8 + kSlotBytes;
@@ -113,10 +127,11 @@ struct Cfg {
   static_assert(kSlots <= 32, "a warp expands its slots one per lane");
   static_assert(kCtasPerSm >= 1, "one CTA's shared memory fits an SM");
 };
-// Segments per row that every k fits in either shape's merge.
-constexpr int kMaxSeg = Cfg<256>::kMergeEntries / Cfg<256>::kMaxK < Cfg<512>::kMergeEntries / Cfg<512>::kMaxK
-                            ? Cfg<256>::kMergeEntries / Cfg<256>::kMaxK
-                            : Cfg<512>::kMergeEntries / Cfg<512>::kMaxK;
+// Segments per row that every k fits in every shape's merge.
+template <int NT, int EB>
+constexpr int seg_cap() { return Cfg<NT, EB>::kMergeEntries / Cfg<NT, EB>::kMaxK; }
+constexpr int min2(int a, int b) { return a < b ? a : b; }
+constexpr int kMaxSeg = min2(min2(seg_cap<256, 4>(), seg_cap<256, 2>()), min2(seg_cap<512, 4>(), seg_cap<512, 2>()));
 
 // Radix digits of D bits over the 64-bit composite, most significant first (the last digit takes what is left).
 template <int D>
@@ -384,7 +399,7 @@ __device__ __forceinline__ int record(const TileRegs<T, NT, U>& t, float f_lo, u
     if (bal == 0u) continue;
     if (maybe) {
       const int pos = wcnt + __popc(bal & below);
-      if (pos < Cfg<NT>::kSlots) {
+      if (pos < Cfg<NT, sizeof(T)>::kSlots) {
         wslot[pos] = t.r[u];
         widx[pos] = (unsigned)v;
       }
@@ -567,7 +582,7 @@ __device__ __forceinline__ void emit(const SegArgs& a, long long row, int j, u64
 // the body's first aligned address go with segment 0, those after its end with the last segment.
 template <typename T, int NT>
 __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const SegArgs a) {
-  using C = Cfg<NT>;
+  using C = Cfg<NT, sizeof(T)>;
   constexpr int V = VecN<T>::N;
   constexpr int kThreads = NT, kWarps = C::kWarps, kU = C::kU, kStages = C::kStages, kTileVecs = C::kTileVecs;
   constexpr int kRingBytes = C::kRingBytes, kMergeEntries = C::kMergeEntries;
@@ -654,7 +669,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   // The fraction of the segment in tiles 0..j.
   const float seg_elems = (float)nv * V + (float)nextra;
   auto seen_after = [&](int j) {
-    return ((float)min(nv, (j + 1) * kTileVecs) * V + (float)nextra) / seg_elems;
+    return seg_elems > 0.0f ? ((float)min(nv, (j + 1) * kTileVecs) * V + (float)nextra) / seg_elems : 1.0f;
   };
 
   // Pass 0 speculates: the bound rises to the m-th largest composite seen so far (m sized so that the whole segment
@@ -930,7 +945,8 @@ cudaError_t prepare_stream_kernel() {
   if (e != cudaSuccess) return e;
   const unsigned long long bit = 1ull << (dev & 63);
   if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
-  e = cudaFuncSetAttribute(topk_stream<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<NT>::kSmemBytes);
+  e = cudaFuncSetAttribute(topk_stream<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           Cfg<NT, sizeof(T)>::kSmemBytes);
   if (e != cudaSuccess) return e;
   done.fetch_or(bit, std::memory_order_acq_rel);
   return cudaSuccess;
@@ -943,7 +959,7 @@ int start_shape(const SegArgs& a, long long rows, long long nseg, cudaStream_t s
     cudaGetLastError();
     return (int)e;
   }
-  topk_stream<T, NT><<<dim3((unsigned)nseg, (unsigned)rows), NT, Cfg<NT>::kSmemBytes, s>>>(a);
+  topk_stream<T, NT><<<dim3((unsigned)nseg, (unsigned)rows), NT, Cfg<NT, sizeof(T)>::kSmemBytes, s>>>(a);
   return (int)cudaGetLastError();
 }
 
@@ -960,7 +976,8 @@ bool bad_args(const void* x, long long rows, long long cols, int k, long long ch
   if (k > cols || k > kMaxK || cols > INT_MAX / 2 || rows > 65535 || chunk <= 0) return true;
   if (reinterpret_cast<uintptr_t>(x) % (uintptr_t)elem) return true;
   if (chunk > cols) chunk = cols;
-  const long long cap = narrow_for(rows, k) ? Cfg<256>::kMergeEntries : Cfg<512>::kMergeEntries;
+  const long long cap = narrow_for(rows, k) ? (elem == 4 ? Cfg<256, 4>::kMergeEntries : Cfg<256, 2>::kMergeEntries)
+                                            : (elem == 4 ? Cfg<512, 4>::kMergeEntries : Cfg<512, 2>::kMergeEntries);
   return segments(cols, chunk) * k > cap;
 }
 
@@ -1093,8 +1110,9 @@ cudaError_t noalloc_scratch(void** out) {
 
 // The top-k of launch() without any caller-provided workspace or counters (no counterpart in the reference): values
 // [rows, k] in x's dtype and int64 indices [rows, k] of x [rows, cols], dtype 0 (fp32) or 1 (bf16), planned as plan()
-// would with min_chunk 2048. Allocates nothing. Returns 0, -1 for arguments launch() would also reject, -2 when the
-// plan needs more than the static scratch holds (rows * segments * k > 491,520 or rows > 65,536), or a cudaError_t.
+// would with min_chunk 2048, except that a plan whose split rows would need more than the scratch's 491,520
+// composites of workspace runs each row in one piece. Allocates nothing. Returns 0, -1 for arguments launch() would
+// also reject, -2 for more than 65,536 rows (the scratch's counters), or a cudaError_t.
 // The first call on a device looks up the scratch address (make it before any stream capture). Every call shares the
 // one scratch array, so calls that overlap on the GPU (different streams, no ordering between them) race; calls on
 // one stream are ordered. The counters are cleared on the caller's stream at each call.
@@ -1106,8 +1124,9 @@ CKB_EXPORT int ckb_topk_launch_noalloc(const void* x, void* values, void* indice
   long long chunk = plan_seg(rows, cols, elem, 2048);
   if (bad_args(x, rows, cols, k, chunk, elem)) return -1;
   if (chunk > cols) chunk = cols;
-  const long long nseg = segments(cols, chunk);
-  if (rows > 2 * kNoAllocCounterWords || (nseg > 1 && rows * nseg * k > kNoAllocWorkWords)) return -2;
+  long long nseg = segments(cols, chunk);
+  if (nseg > 1 && rows * nseg * k > kNoAllocWorkWords) nseg = 1;  // whole rows: no workspace at all
+  if (rows > 2 * kNoAllocCounterWords) return -2;
   void* base = nullptr;
   cudaError_t e = noalloc_scratch(&base);
   if (e != cudaSuccess) return (int)e;

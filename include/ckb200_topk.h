@@ -37,14 +37,16 @@ int ckb_topk_merge_launch(const unsigned long long* lists, int nlists, void* val
  * through its own fixed-budget allocator, or a path that cannot afford cudaMalloc's device synchronisation): no
  * workspace or counters are passed; a 4 MiB scratch array compiled into this library (held on every GPU that loads
  * it, until exit) serves instead. No counterpart in the reference. dtype 0 fp32 / 1 bf16; returns -1 for arguments
- * launch() rejects, -2 when rows * chunks * k > 491,520 or rows > 65,536 (the scratch is too small). The first call on
- * a device looks up the scratch address: make it before any stream capture. All calls share the scratch, so calls
- * that overlap on the GPU race; the counters are cleared on `stream` at every call. */
+ * launch() rejects, -2 for more than 65,536 rows (beyond the scratch's counters; launch() rejects those anyway). A
+ * plan whose split rows would need more workspace than the scratch's 491,520 composites runs each row in one piece
+ * instead. The first call on a device looks up the scratch address: make it before any stream capture. All calls
+ * share the scratch, so calls that overlap on the GPU race; the counters are cleared on `stream` at every call. */
 int ckb_topk_launch_noalloc(const void* x, void* values, void* indices, long long rows, long long cols, int k,
                             int dtype, cudaStream_t stream);
 
-/* Bounded-wait status of this library's kernels since the last reset: 0 fine, 1 a bulk-copy wait gave up.
- * Synchronous; reset != 0 clears it; negative: -cudaError_t. No counterpart in the reference. */
+/* Status word of this library's kernels since the last reset (0 fine; the streaming kernel waits only on its own
+ * asynchronous copies, which always complete, so nothing sets it today). Synchronous; reset != 0 clears it; negative:
+ * -cudaError_t. No counterpart in the reference. */
 int ckb_topk_status(int reset);
 
 #ifdef __cplusplus

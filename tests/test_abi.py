@@ -75,8 +75,8 @@ def test_rejected_arguments_return_minus_one():
 
 def test_topk_plan_host_logic():
     """plan() needs no GPU: a row splits into at most 12 segments (so any k <= 512 fits the last CTA's merge), each at
-    least min_chunk columns. The headline batch (512 rows, fewer than the 592 CTAs of 256 threads that 148 SMs hold
-    at once) streams one CTA per row in a single wave; a small batch splits its rows to fill the GPU."""
+    least min_chunk columns. The headline batch (512 rows, at least two per SM) runs one CTA per row; a small batch
+    splits its rows to fill the GPU."""
     tk = _native.load("topk")
     for rows, cols, dt in ((512, 151936, 0), (64, 151936, 0), (1, 128256, 0), (512, 32000, 1), (3, 50, 0)):
         chunk = tk.plan(rows, cols, dt, 256, 4, 2048)
@@ -85,19 +85,20 @@ def test_topk_plan_host_logic():
         assert nseg <= 12
         if nseg > 1:
             assert chunk >= 2048
-    assert tk.plan(512, 151936, 0, 256, 4, 2048) == 151936
+    assert tk.plan(512, 151936, 0, 256, 4, 2048) == 151936  # one CTA per row
     assert -(-151936 // tk.plan(64, 151936, 0, 256, 4, 2048)) > 1
     assert tk.plan(3, 50, 0, 256, 4, 2048) == 50
 
 
-def test_noalloc_plans_always_fit_the_scratch():
-    """ckb_topk_launch_noalloc plans as plan(rows, cols, dtype, ..., 2048) does. A row is split only when the batch
-    has fewer rows than two per SM, into about one CTA per SM in all, so rows * segments * k stays far below the
-    491,520 composites of its scratch for every k <= 512: its -2 (scratch too small) is a guard that no plan reaches."""
+def test_noalloc_split_plans_stay_small():
+    """Below two rows per SM a row is split into about one CTA per SM in all, so rows * segments * k stays within the
+    no-allocation entry's 491,520-composite scratch for every k <= 512; larger batches keep rows whole."""
     tk = _native.load("topk")
-    for rows in (1, 2, 3, 7, 64, 100, 147, 148, 200, 295, 296, 1000, 65535):
+    for rows in (1, 2, 3, 7, 64, 100, 147, 148, 200, 295):
         for cols in (1000, 4096, 151936, 1 << 20, 1 << 26):
             for dt in (0, 1):
                 chunk = tk.plan(rows, cols, dt, 256, 4, 2048)
                 nseg = -(-cols // chunk)
                 assert nseg == 1 or rows * nseg * 512 <= 491520, (rows, cols, nseg)
+    for rows in (296, 512, 1000, 65535):
+        assert tk.plan(rows, 151936, 0, 256, 4, 2048) == 151936

@@ -123,6 +123,19 @@ def test_increasing_rows_overflow_every_tile(dtype):
         _check(x, k, vv, ii, f"monotone k={k}")
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("nseg", [1, 2, 3, 5])
+def test_wide_batch_segments(dtype, nseg):
+    """A batch with at least two rows per SM (the 256-thread shape) with rows kept whole or split into nseg segments
+    that the row's last finisher merges. Odd columns make every row's alignment differ."""
+    g = torch.Generator().manual_seed(nseg)
+    x = (torch.randn(400, 40001, generator=g) * 3).to(dtype)
+    xd = x.cuda()
+    v, i, counters = _launch_with_chunk(xd, 50, -(-x.shape[1] // nseg))
+    _check(x, 50, v, i, f"{nseg} segments")
+    assert int(counters.abs().sum()) == 0
+
+
 def test_repeated_calls_reuse_workspace_and_counters():
     x = workloads.topk_512x151936(scale=8)["x"].cuda()
     first = topk.topk(x, 50)

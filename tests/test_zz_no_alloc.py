@@ -66,3 +66,16 @@ def test_split_rows_merge_through_the_scratch_call_after_call(dtype):
         torch.cuda.synchronize()
         assert torch.equal(i, want_i), f"call {call}: indices differ"
         assert bits_equal(v, want_v), f"call {call}: values differ"
+
+
+def test_large_batch_keeps_rows_whole_within_the_scratch():
+    """4096 rows (a batch of many short rows, one CTA each, no workspace): equals launch()."""
+    fn = _noalloc()
+    g = torch.Generator().manual_seed(11)
+    x = (torch.randn(4096, 8192, generator=g) * 3).cuda()
+    want_v, want_i = topk.topk(x, 50)
+    v = torch.empty(4096, 50, device="cuda")
+    i = torch.empty(4096, 50, dtype=torch.int64, device="cuda")
+    assert fn(x.data_ptr(), v.data_ptr(), i.data_ptr(), 4096, 8192, 50, 0, torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(i, want_i) and bits_equal(v, want_v)
