@@ -273,7 +273,7 @@ def make_case(name, impl="ours", seeded=True, sets=2):
                 return lib.launch(q.data_ptr(), k.data_ptr(), cos.data_ptr(), sin.data_ptr(), ids.data_ptr(),
                                   qo[i % sets].data_ptr(), ko[i % sets].data_ptr(), 32768, 32, 8, 128, 1, 0, 40, 1,
                                   stream)
-        return Case(name, nbytes, rows, launch, sets, None, "rope_vec")
+        return Case(name, nbytes, rows, launch, sets, None, "rope_tokens")
 
     if name == "topk_512x151936":
         x0 = workloads.topk_512x151936()["x"].to(dev) if seeded else dev_randn(512, 151936, scale=3.0)
@@ -298,7 +298,7 @@ def make_case(name, impl="ours", seeded=True, sets=2):
             return lib.launch(xs[i % sets].data_ptr(), vals.data_ptr(), idx.data_ptr(), work.data_ptr(),
                               counters.data_ptr(), 512, 151936, 50, 0, 256, 4, chunk, stream)
 
-        return Case(name, nbytes, rows, launch, sets, None, "topk_chunk")
+        return Case(name, nbytes, rows, launch, sets, None, "topk_stream")
     raise SystemExit(f"unknown workload {name}")
 
 

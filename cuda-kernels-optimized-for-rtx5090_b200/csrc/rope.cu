@@ -54,7 +54,7 @@ __device__ __forceinline__ uint4 ld_x(const void* p) {
 
 // kCache: cos/sin from the cache (C its dtype); otherwise sincosf(pos * inv_freq[i]).
 template <typename T, typename C, bool kCache, bool kInPlace>
-__global__ void __launch_bounds__(256, CKB_ROPE_MIN_BLOCKS) rope_vec(const T* q, const T* k, const C* __restrict__ cos_rows,
+__global__ void __launch_bounds__(256, CKB_ROPE_MIN_BLOCKS) rope_tokens(const T* q, const T* k, const C* __restrict__ cos_rows,
                                                 const C* __restrict__ sin_rows, const float* __restrict__ inv_freq,
                                                 const long long* __restrict__ ids, T* q_out, T* k_out,
                                                 long long tokens, int q_heads, int kv_heads, int head_dim) {
@@ -195,11 +195,11 @@ int start(const Args& a, cudaStream_t s) {
     if (grid > INT_MAX) return -1;
     const dim3 block(lanes, r, z);
     if (in_place) {
-      rope_vec<T, C, kCache, true><<<(unsigned)grid, block, 0, s>>>(
+      rope_tokens<T, C, kCache, true><<<(unsigned)grid, block, 0, s>>>(
           (const T*)a.q, (const T*)a.k, (const C*)a.cos_rows, (const C*)a.sin_rows, a.inv_freq, a.ids, (T*)a.q_out,
           (T*)a.k_out, a.tokens, a.q_heads, a.kv_heads, a.head_dim);
     } else {
-      rope_vec<T, C, kCache, false><<<(unsigned)grid, block, 0, s>>>(
+      rope_tokens<T, C, kCache, false><<<(unsigned)grid, block, 0, s>>>(
           (const T*)a.q, (const T*)a.k, (const C*)a.cos_rows, (const C*)a.sin_rows, a.inv_freq, a.ids, (T*)a.q_out,
           (T*)a.k_out, a.tokens, a.q_heads, a.kv_heads, a.head_dim);
     }
