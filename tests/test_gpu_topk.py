@@ -136,6 +136,29 @@ def test_wide_batch_segments(dtype, nseg):
     assert int(counters.abs().sum()) == 0
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("k", [50, 64, 65])
+def test_many_rows_edge_cases(dtype, k):
+    """300 rows (at least two per SM: the 256-thread shape, and for k <= 64 its warp-local variant) mixing random
+    rows, few-valued rows (ties everywhere), rising and falling rows (a tile overflowing a warp's slots; a speculative
+    bound above the final k-th), constant rows and rows with infinities and NaN: every one bit-exact."""
+    g = torch.Generator().manual_seed(k)
+    cols = 20001
+    x = torch.randn(300, cols, generator=g) * 3
+    up = torch.arange(cols, dtype=torch.float32)
+    for r in range(0, 300, 10):
+        x[r + 1] = torch.randint(-3, 4, (cols,), generator=g).float()
+        x[r + 2] = up
+        x[r + 3] = up.flip(0)
+        x[r + 4] = 1.5
+        x[r + 5, r] = float("inf")
+        x[r + 5, r + 7] = float("-inf")
+        x[r + 6, 100 + r] = float("nan")
+    x = x.to(dtype)
+    vv, ii = topk.topk(x.cuda(), k)
+    _check(x, k, vv, ii, f"many rows k={k}")
+
+
 def test_repeated_calls_reuse_workspace_and_counters():
     x = workloads.topk_512x151936(scale=8)["x"].cuda()
     first = topk.topk(x, 50)
