@@ -7,19 +7,21 @@
 //     every lane keeps NV vectors of its row in registers; group-local shuffles, no barrier;
 //   * block path, rows of at most 32768 fp32 / bf16 values: one block per row, 32 values per thread in
 //     registers, two barriers per row;
-//   * cluster path, longer rows: a row is split over a thread-block cluster of CL CTAs (2..16); the grid holds as many
-//     clusters as stay resident and each loops over its rows. Every CTA pulls its own slice of a row into its own
-//     shared memory with a bulk copy (cp.async.bulk on an mbarrier) issued up to 4 rows ahead (a ring of slice
-//     buffers), the CTAs exchange the max and then the sum through distributed shared memory, and each CTA
-//     normalises from shared memory. No copy is multicast;
-//   * wide cluster path, rows whose slices exceed shared memory: the same split and exchange, each CTA reading its
-//     slice twice from global memory (online max/sum, then normalise; the second read mostly from L2);
+//   * cluster path, longer rows: a row is split over a thread-block cluster of CL CTAs (2..16), one row per cluster
+//     (a resident set of clusters loops over the rows only beyond the grid's y limit). Every CTA pulls its own slice
+//     of the row into its own shared memory with a bulk copy (cp.async.bulk on an mbarrier), takes the slice's max
+//     and exp(x - max) in place, and the CTAs exchange one (max, sum) pair each through distributed shared memory;
+//     each CTA scales from shared memory. No copy is multicast;
+//   * streaming cluster path, rows whose slices exceed shared memory: the same split and single exchange, each CTA
+//     reading its slice twice from global memory (a running max and sum per warp, then exp(x - M) / S; the second
+//     read comes from L2);
 //   * stream path (unaligned pointers, cols not a multiple of the vector): one block per row reading the row three
 //     times (max, sum, normalise; the later reads mostly from L2).
-// Accuracy (fp32 outputs within 1e-6 relative of an fp64 softmax, elementwise): exp(x - max) uses CUDA's expf on the
-// fp32 difference and folds the difference's rounding error back in (TwoSum), each thread sums its exponentials
-// pairwise per 16-byte vector into an fp64 accumulator and the cross-thread reductions run in fp64; the output is
-// e * (float)(1 / sum).
+// Accuracy (fp32 outputs within 1e-6 relative of an fp64 softmax, elementwise): the group and block paths take
+// exp(x - max) with CUDA's expf on the fp32 difference and fold the difference's rounding error back in (TwoSum);
+// the cluster paths use exp_pair below (relative error within 2.1e-7, measured over every argument). Each thread sums
+// its exponentials pairwise per 16-byte vector into an fp64 accumulator, cross-thread and cross-CTA reductions run in
+// fp64, and the output is e * (float)(1 / sum) (or e * (float)(exp(m_c - M) / S) per cluster slice).
 #include "ckb200_softmax.h"
 #include "common.cuh"
 
@@ -51,6 +53,61 @@ __device__ __forceinline__ float exp_shifted(float x, float m) {
   const float lo = (x - (d - bv)) + (-m - bv);
   const float e = expf(d);
   return e > 0.0f ? fmaf(e, lo, e) : e;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Packed exponentials for the cluster path: exp(x - M) for two values at a time on the fp32x2 pipe (sm_100).
+// Method (from the mathematics; no library routine is restated): TwoSum (Knuth) splits x - M into s + lo exactly;
+// th = s * log2(e) rounded to fp32; E = 2^th by the ex2.approx instruction (flushes results below FLT_MIN to zero);
+// the residual r = (s + lo) - th * ln 2, with ln 2 as a float pair so that r is exact to far below an ulp of E and
+// |r| < 1e-5, is folded in as E * (1 + r) (the dropped r^2 / 2 term is below 1e-10). The relative error is that of
+// ex2.approx plus one rounding. Before the split x is raised to `lowc`, a value below M whose exponential is zero, so
+// that x = -inf gives 0 instead of the inf - inf of the split; a NaN or +inf max makes lowc NaN and every result NaN.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+template <int WIDTH = 32>
+__device__ __forceinline__ float warp_max_nan(float v) {
+#pragma unroll
+  for (int o = WIDTH / 2; o > 0; o >>= 1) v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float ex2_ftz(float a) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(a));
+  return r;
+}
+
+struct ExpShift {
+  float2 nm;   // (-M, -M)
+  float lowc;  // every x below it has exp(x - M) == 0 in fp32
+  __device__ __forceinline__ explicit ExpShift(float M) {
+    nm = make_float2(-M, -M);
+    lowc = M - fmaxf(150.0f, fabsf(M) * 0x1p-20f);
+  }
+};
+
+__device__ __forceinline__ float2 exp_pair(float2 x, const ExpShift& e) {
+  const float2 kNeg1 = make_float2(-1.0f, -1.0f);
+  const float2 kL2E = make_float2(1.44269502162933349609375f, 1.44269502162933349609375f);  // fp32(log2 e)
+  const float2 kNLn2Hi = make_float2(-0.693147182464599609375f, -0.693147182464599609375f);  // -fp32(ln 2)
+  const float2 kNLn2Lo = make_float2(1.904654323148236e-09f, 1.904654323148236e-09f);       // -(ln 2 - fp32(ln 2))
+  x.x = fmaxf(x.x, e.lowc);
+  x.y = fmaxf(x.y, e.lowc);
+  const float2 s = __fadd2_rn(x, e.nm);
+  const float2 xb = __ffma2_rn(e.nm, kNeg1, s);  // s - (-M): x as rounded into s
+  const float2 mb = __ffma2_rn(xb, kNeg1, s);    // s - xb: -M as rounded into s
+  const float2 dx = __ffma2_rn(xb, kNeg1, x);    // x - xb
+  const float2 dm = __ffma2_rn(mb, kNeg1, e.nm); // -M - mb
+  const float2 lo = __fadd2_rn(dx, dm);          // s + lo == x - M exactly
+  const float2 th = __fmul2_rn(s, kL2E);
+  const float2 E = make_float2(ex2_ftz(th.x), ex2_ftz(th.y));
+  float2 r = __ffma2_rn(th, kNLn2Hi, s);          // s - th * ln2_hi, exact but for one tiny rounding
+  r = __fadd2_rn(r, __ffma2_rn(th, kNLn2Lo, lo)); // + lo - th * ln2_lo
+  return __ffma2_rn(E, r, E);
 }
 
 // Pairwise sum of the values of one 16-byte vector.
@@ -164,10 +221,12 @@ __global__ void __launch_bounds__(MAXT) sm_block(const T* __restrict__ x, T* __r
 }
 
 // ---------------------------------------------------------------------------------------------- cluster path ----
-constexpr int kClusterThreads = 512;
+constexpr int kClusterThreads = 256;
 constexpr int kMaxStages = 4;
 
-__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+// The start-up handshake: the initialising thread's fence.mbarrier_init (release, cluster scope) already publishes the
+// mbarrier initialisation, so the arrive is relaxed (a release arrive would make every warp wait on a memory fence).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
 // Block-wide max / sum of one value per thread through `red` (32 slots); every thread gets the same result.
@@ -214,21 +273,25 @@ constexpr int kMaxCluster = 16;
 // Grid (CL, G), cluster (CL, 1, 1): cluster g handles rows g, g + G, g + 2G, ... and CTA `rank` owns elements
 // [rank * slice, min((rank + 1) * slice, cols)) of each (slice and cols multiples of the 16-byte vector). A CTA cycles
 // its rows through `stages` slice buffers in dynamic shared memory (stride `stage_vec` 16-byte vectors): the bulk copy
-// of a row is issued `stages` rows ahead. Per row: max over the slice -> every CTA st.asyncs its max to every peer ->
-// exp and sum -> the same for the sums -> normalise and store. The exchange slots and their mbarriers are double
-// buffered by row parity, so a fast CTA's next row never lands in a slot a slow peer still reads.
+// of a row is issued `stages` rows ahead. Per row: the slice's max m_c -> exp(x - m_c) in place (fp32) and their sum
+// s_c -> warp 0 st.asyncs (m_c, s_c) to every peer -> warp 0 combines the cluster's pairs in fp64 into the row max M,
+// the row sum S = sum of s_l * exp(m_l - M) and this slice's scale exp(m_c - M) / S, broadcast through shared memory
+// -> every thread scales and stores. One exchange per row, and no thread waits for the row max before its
+// exponentials. The exchange slots and their mbarrier are double buffered by row parity, so a fast CTA's next row
+// never lands in a slot a slow peer still reads.
 template <typename T>
-__global__ void __launch_bounds__(kClusterThreads) sm_cluster(const T* __restrict__ x, T* __restrict__ y,
+__global__ void __launch_bounds__(kClusterThreads, 3) sm_cluster(const T* __restrict__ x, T* __restrict__ y,
                                                               long long rows, long long cols, int slice,
                                                               int stages, int stage_vec) {
   constexpr int V = VecN<T>::N;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t bars[kMaxStages];
-  __shared__ __align__(8) uint64_t bar_max[2], bar_sum[2];
+  __shared__ __align__(8) uint64_t bar_pair[2];
   __shared__ float xmax[2][kMaxCluster];
   __shared__ double xsum[2][kMaxCluster];
   __shared__ float red[32];
   __shared__ double red_d[32];
+  __shared__ float scale;
 
   cg::cluster_group cluster = cg::this_cluster();
   const unsigned rank = cluster.block_rank();
@@ -243,10 +306,8 @@ __global__ void __launch_bounds__(kClusterThreads) sm_cluster(const T* __restric
 
   if (threadIdx.x == 0) {
     for (int st = 0; st < stages; ++st) mbar_init(&bars[st], 1);
-    for (int p = 0; p < 2; ++p) {
-      mbar_init(&bar_max[p], 1);
-      mbar_init(&bar_sum[p], 1);
-    }
+    mbar_init(&bar_pair[0], 1);
+    mbar_init(&bar_pair[1], 1);
     mbar_fence_init();
     if (bytes)
       for (int st = 0; st < stages; ++st) {
@@ -257,124 +318,12 @@ __global__ void __launch_bounds__(kClusterThreads) sm_cluster(const T* __restric
         }
       }
   }
-  // Every CTA's exchange mbarriers are initialised before any peer sends to them.
+  // Every CTA's exchange mbarriers are initialised before any peer sends to them: every thread arrives here, and
+  // warp 0, the only one that touches peers, waits for the whole cluster before its first send.
   cluster_arrive();
-  cluster_wait();
 
-  // The peer addresses this thread sends to (threads 0 .. csize-1 each serve one peer).
-  unsigned peer_max[2] = {0u, 0u}, peer_sum[2] = {0u, 0u}, peer_bmax[2] = {0u, 0u}, peer_bsum[2] = {0u, 0u};
-  if (threadIdx.x < csize) {
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      peer_max[p] = mapa_u32(smem_u32(&xmax[p][rank]), threadIdx.x);
-      peer_sum[p] = mapa_u32(smem_u32(&xsum[p][rank]), threadIdx.x);
-      peer_bmax[p] = mapa_u32(smem_u32(&bar_max[p]), threadIdx.x);
-      peer_bsum[p] = mapa_u32(smem_u32(&bar_sum[p]), threadIdx.x);
-    }
-  }
-
-  bool ok = true;
-  int t = 0;
-  for (long long row = first; row < rows; row += step, ++t) {
-    const int st = t % stages;
-    const int p = t & 1;
-    const unsigned xphase = (unsigned)(t >> 1) & 1u;
-    uint4* const buf = buf0 + (size_t)st * stage_vec;
-    if (threadIdx.x == 0) {
-      mbar_arrive_expect_tx(&bar_max[p], csize * 4u);
-      mbar_arrive_expect_tx(&bar_sum[p], csize * 8u);
-    }
-    if (bytes) ok = mbar_wait(&bars[st], (unsigned)(t / stages) & 1u) && ok;
-
-    // Pass 1: this slice's max, sent to every CTA of the cluster; the row's max from the cluster's.
-    float m = -CUDART_INF_F;
-    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-      float f[V];
-      unpack16(buf[i], f, x);
-#pragma unroll
-      for (int j = 0; j < V; ++j) m = fmaxf(m, f[j]);
-    }
-    m = block_max(m, red);
-    if (threadIdx.x < csize)
-      st_async_u32(p ? peer_max[1] : peer_max[0], __float_as_uint(m), p ? peer_bmax[1] : peer_bmax[0]);
-    ok = mbar_wait(&bar_max[p], xphase) && ok;
-    m = xmax[p][0];
-    for (unsigned r = 1; r < csize; ++r) m = fmaxf(m, xmax[p][r]);
-
-    // Pass 2: sum of exp(x - max); fp32 slices keep the exponentials in place for pass 3.
-    double sum = 0.0;
-    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-      float f[V];
-      unpack16(buf[i], f, x);
-      sum += (double)exp_vec(f, m);
-      if constexpr (V == 4) buf[i] = pack16(f, x);
-    }
-    sum = block_sum(sum, red_d);
-    if (threadIdx.x < csize)
-      st_async_u64(p ? peer_sum[1] : peer_sum[0], (unsigned long long)__double_as_longlong(sum),
-                   p ? peer_bsum[1] : peer_bsum[0]);
-    ok = mbar_wait(&bar_sum[p], xphase) && ok;
-    double total = 0.0;
-    for (unsigned r = 0; r < csize; ++r) total += xsum[p][r];
-    const float inv = (float)(1.0 / total);
-
-    // Pass 3: normalise from shared memory, stream to HBM.
-    T* dst = y + row * cols + beg;
-    for (int i = threadIdx.x; i < nv; i += blockDim.x) {
-      float f[V];
-      unpack16(buf[i], f, x);
-      if constexpr (V == 4) {
-#pragma unroll
-        for (int j = 0; j < V; ++j) f[j] *= inv;
-      } else {
-#pragma unroll
-        for (int j = 0; j < V; ++j) f[j] = exp_shifted(f[j], m) * inv;
-      }
-      store16(reinterpret_cast<T*>(reinterpret_cast<uint4*>(dst) + i), f);
-    }
-    // Every thread is done with this buffer (and with red / red_d): refill it `stages` rows ahead.
-    fence_proxy_async();
-    __syncthreads();
-    if (threadIdx.x == 0 && bytes) {
-      const long long r = row + (long long)stages * step;
-      if (r < rows) {
-        mbar_arrive_expect_tx(&bars[st], bytes);
-        bulk_load(buf, x + r * cols + beg, bytes, &bars[st]);
-      }
-    }
-  }
-  if (!ok) atomicOr(&g_softmax_status, CKB_STATUS_TIMEOUT);
-}
-
-// Rows whose slices do not fit shared memory: the same cluster split and st.async exchange, but each CTA reads its
-// slice from global memory twice -- an online (max, sum) pass, then the normalising pass, whose reads mostly hit L2
-// (the resident CTAs' slices fit in it). The per-thread running sum is fp64 and is rescaled in fp64 when the running
-// max grows; the CTAs' (max, sum) pairs combine in fp64.
-template <typename T>
-__global__ void __launch_bounds__(kClusterThreads) sm_cluster_wide(const T* __restrict__ x, T* __restrict__ y,
-                                                                   long long rows, long long cols, long long slice) {
-  constexpr int V = VecN<T>::N;
-  __shared__ __align__(8) uint64_t bar_pair[2];
-  __shared__ float xmax[2][kMaxCluster];
-  __shared__ double xsum[2][kMaxCluster];
-  __shared__ float red[32];
-  __shared__ double red_d[32];
-  __shared__ float row_max;
-
-  cg::cluster_group cluster = cg::this_cluster();
-  const unsigned rank = cluster.block_rank();
-  const unsigned csize = cluster.num_blocks();
-  const long long beg = rank * slice;
-  long long n = cols - beg;
-  n = n < 0 ? 0 : (n > slice ? slice : n);
-  const long long nv = n / V;
-  if (threadIdx.x == 0) {
-    mbar_init(&bar_pair[0], 1);
-    mbar_init(&bar_pair[1], 1);
-    mbar_fence_init();
-  }
-  cluster_arrive();
-  cluster_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  // The peer addresses lane l of warp 0 sends to (lanes 0 .. csize-1 each serve one peer).
   unsigned peer_max[2] = {0u, 0u}, peer_sum[2] = {0u, 0u}, peer_bar[2] = {0u, 0u};
   if (threadIdx.x < csize) {
 #pragma unroll
@@ -384,67 +333,273 @@ __global__ void __launch_bounds__(kClusterThreads) sm_cluster_wide(const T* __re
       peer_bar[p] = mapa_u32(smem_u32(&bar_pair[p]), threadIdx.x);
     }
   }
+
+  bool ok = true;
+  int t = 0;
+  for (long long row = first; row < rows; row += step, ++t) {
+    const int st = t % stages;
+    const int p = t & 1;
+    uint4* const buf = buf0 + (size_t)st * stage_vec;
+    if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar_pair[p], csize * 12u);
+    if (bytes) ok = mbar_wait(&bars[st], (unsigned)(t / stages) & 1u) && ok;
+
+    // Pass 1: the slice's max m_c (NaN-propagating), folded by every warp from the per-warp maxima.
+    float m = -CUDART_INF_F;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < nv; i += kClusterThreads) {
+      float f[V];
+      unpack16(buf[i], f, x);
+#pragma unroll
+      for (int j = 0; j < V; ++j) m = max_nan(m, f[j]);
+    }
+    m = warp_max_nan(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    const float mc = warp_max_nan(lane < warps ? red[lane] : -CUDART_INF_F);
+    // A slice of -inf only takes its (zero) exponentials against 0; its pair still reports m_c = -inf.
+    const ExpShift es(mc == -CUDART_INF_F ? 0.0f : mc);
+
+    // Pass 2: exp(x - m_c), summed pairwise per vector into fp64; fp32 slices keep the exponentials in place.
+    double sum = 0.0;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < nv; i += kClusterThreads) {
+      const uint4 raw = buf[i];
+      if constexpr (V == 4) {
+        const float2 a = exp_pair(make_float2(__uint_as_float(raw.x), __uint_as_float(raw.y)), es);
+        const float2 b = exp_pair(make_float2(__uint_as_float(raw.z), __uint_as_float(raw.w)), es);
+        const float2 ab = __fadd2_rn(a, b);
+        sum += (double)(ab.x + ab.y);
+        buf[i] = make_uint4(__float_as_uint(a.x), __float_as_uint(a.y), __float_as_uint(b.x), __float_as_uint(b.y));
+      } else {
+        float f[V];
+        unpack16(raw, f, x);
+        float2 e[V / 2];
+#pragma unroll
+        for (int j = 0; j < V / 2; ++j) e[j] = exp_pair(make_float2(f[2 * j], f[2 * j + 1]), es);
+        const float2 s01 = __fadd2_rn(e[0], e[1]), s23 = __fadd2_rn(e[2], e[3]);
+        const float2 s03 = __fadd2_rn(s01, s23);
+        sum += (double)(s03.x + s03.y);
+      }
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) red_d[warp] = sum;
+    __syncthreads();
+
+    // Exchange and combine (warp 0): M = max m_l, S = sum s_l * exp(m_l - M) in fp64, scale = exp(m_c - M) / S.
+    // A NaN or +inf anywhere in the row, or a row of -inf, makes M, S or the scale NaN, so the row is all NaN.
+    if (warp == 0) {
+      const double sc = warp_sum(lane < warps ? red_d[lane] : 0.0);
+      if (t == 0) cluster_wait();
+      if (lane < (int)csize) {
+        st_async_u32(p ? peer_max[1] : peer_max[0], __float_as_uint(mc), p ? peer_bar[1] : peer_bar[0]);
+        st_async_u64(p ? peer_sum[1] : peer_sum[0], (unsigned long long)__double_as_longlong(sc),
+                     p ? peer_bar[1] : peer_bar[0]);
+      }
+      ok = mbar_wait(&bar_pair[p], (unsigned)(t >> 1) & 1u) && ok;
+      const float ml = lane < (int)csize ? xmax[p][lane] : -CUDART_INF_F;
+      const float M = warp_max_nan(ml);
+      const double w = lane < (int)csize ? exp((double)ml - (double)M) : 0.0;
+      const double S = warp_sum(lane < (int)csize ? xsum[p][lane] * w : 0.0);
+      const double wc = __shfl_sync(0xffffffffu, w, (int)rank);
+      if (lane == 0) scale = (float)(wc / S);
+    }
+    __syncthreads();
+    const float f_scale = scale;
+    const float2 scale2 = make_float2(f_scale, f_scale);
+
+    // Pass 3: scale from shared memory, stream to HBM.
+    uint4* const dst = reinterpret_cast<uint4*>(y + row * cols + beg);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < nv; i += kClusterThreads) {
+      const uint4 raw = buf[i];
+      if constexpr (V == 4) {
+        const float2 a = __fmul2_rn(make_float2(__uint_as_float(raw.x), __uint_as_float(raw.y)), scale2);
+        const float2 b = __fmul2_rn(make_float2(__uint_as_float(raw.z), __uint_as_float(raw.w)), scale2);
+        st_stream(dst + i, make_uint4(__float_as_uint(a.x), __float_as_uint(a.y), __float_as_uint(b.x),
+                                      __float_as_uint(b.y)));
+      } else {
+        float f[V];
+        unpack16(raw, f, x);
+#pragma unroll
+        for (int j = 0; j < V / 2; ++j) {
+          const float2 e = __fmul2_rn(exp_pair(make_float2(f[2 * j], f[2 * j + 1]), es), scale2);
+          f[2 * j] = e.x;
+          f[2 * j + 1] = e.y;
+        }
+        store16(reinterpret_cast<T*>(dst + i), f);
+      }
+    }
+    // Refill this buffer `stages` rows ahead once every thread is done with it (the exponentials written into it by
+    // the generic proxy are ordered before the bulk copy's writes by the proxy fence). With no row left for the
+    // buffer, the CTA just finishes. The barrier also keeps `scale` and `red` from being rewritten while read.
+    const long long next = row + (long long)stages * step;
+    if (next < rows) {
+      if (bytes) fence_proxy_async();
+      __syncthreads();
+      if (threadIdx.x == 0 && bytes) {
+        mbar_arrive_expect_tx(&bars[st], bytes);
+        bulk_load(buf, x + next * cols + beg, bytes, &bars[st]);
+      }
+    }
+  }
+  if (!ok) atomicOr(&g_softmax_status, CKB_STATUS_TIMEOUT);
+}
+
+// ------------------------------------------------------------------------------------ streaming cluster path ----
+// One row per cluster of CL CTAs (2..16) of 512 threads; CTA `rank` owns the 16-byte vectors [rank * sv, (rank + 1) *
+// sv) of the row. Nothing is staged in shared memory: pass A streams the slice from HBM, U vectors per thread in
+// flight, with a running max per warp and exp(x - max) summed per thread (a larger max rescales the sum in fp64);
+// the warps' pairs fold into the CTA's (m_c, s_c), warp 0 st.asyncs it to every peer and combines the cluster's
+// pairs in fp64 into the row max M and sum S; pass B re-reads the slice (from L2: every resident cluster's slices
+// together are a fraction of it) and writes exp(x - M) * (1 / S).
+constexpr int kStreamThreads = 512;
+constexpr int kStreamMaxCluster = 8;  // measured best for 4 MB rows (16-CTA clusters at 2 CTAs/SM pack worse)
+
+__device__ __forceinline__ uint4 neg_inf16(const float*) {
+  return make_uint4(0xff800000u, 0xff800000u, 0xff800000u, 0xff800000u);
+}
+__device__ __forceinline__ uint4 neg_inf16(const __nv_bfloat16*) {
+  return make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+}
+
+template <typename T, int U>
+__global__ void __launch_bounds__(kStreamThreads, 2) sm_cluster_stream(const T* __restrict__ x, T* __restrict__ y,
+                                                                      long long rows, long long cols, long long sv) {
+  constexpr int V = VecN<T>::N;
+  constexpr int kWarps = kStreamThreads / 32;
+  constexpr long long kStep = (long long)kStreamThreads * U;
+  __shared__ __align__(8) uint64_t bar_pair[2];
+  __shared__ float xmax[2][kMaxCluster];
+  __shared__ double xsum[2][kMaxCluster];
+  __shared__ float wmax[kWarps];
+  __shared__ double wsum[kWarps];
+  __shared__ float row_m, row_inv;
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const unsigned rank = cluster.block_rank();
+  const unsigned csize = cluster.num_blocks();
+  const long long nvec = cols / V;
+  const long long vb = (long long)rank * sv < nvec ? (long long)rank * sv : nvec;
+  const long long ve = vb + sv < nvec ? vb + sv : nvec;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint4 fill = neg_inf16(x);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar_pair[0], 1);
+    mbar_init(&bar_pair[1], 1);
+    mbar_fence_init();
+  }
+  // Every thread arrives; warp 0, the only one that touches peers, waits before its first send.
+  cluster_arrive();
+  unsigned peer_max[2] = {0u, 0u}, peer_sum[2] = {0u, 0u}, peer_bar[2] = {0u, 0u};
+  if (threadIdx.x < csize) {
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      peer_max[p] = mapa_u32(smem_u32(&xmax[p][rank]), threadIdx.x);
+      peer_sum[p] = mapa_u32(smem_u32(&xsum[p][rank]), threadIdx.x);
+      peer_bar[p] = mapa_u32(smem_u32(&bar_pair[p]), threadIdx.x);
+    }
+  }
+
   bool ok = true;
   int t = 0;
   for (long long row = blockIdx.y; row < rows; row += gridDim.y, ++t) {
     const int p = t & 1;
     if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar_pair[p], csize * 12u);
-    const uint4* src = reinterpret_cast<const uint4*>(x + row * cols + beg);
-    // Online (max, sum) of this thread's elements.
-    float m = -CUDART_INF_F;
+    const uint4* src = reinterpret_cast<const uint4*>(x + row * cols);
+
+    // Pass A: a running max per warp (mw, the same in every lane) and this thread's sum of exp(x - mw).
+    float mw = -CUDART_INF_F;
     double s = 0.0;
-    for (long long i = threadIdx.x; i < nv; i += blockDim.x) {
-      float f[V];
-      unpack16(__ldg(src + i), f, x);
-      float vm = f[0];
+    for (long long i0 = vb + threadIdx.x; i0 < ve; i0 += kStep) {
+      uint4 r[U];
 #pragma unroll
-      for (int j = 1; j < V; ++j) vm = fmaxf(vm, f[j]);
-      if (vm > m) {
-        if (s != 0.0) s *= exp((double)m - (double)vm);
-        m = vm;
+      for (int u = 0; u < U; ++u) {
+        const long long i = i0 + (long long)u * kStreamThreads;
+        r[u] = i < ve ? __ldg(src + i) : fill;  // -inf past the slice: no effect on the max, exp 0
       }
-      if (m != -CUDART_INF_F) {
-        s += (double)exp_vec(f, m);  // -inf elements add 0, NaN (and inf - inf) poison the sum
-      } else {
+      float cm = -CUDART_INF_F;
 #pragma unroll
-        for (int j = 0; j < V; ++j)
-          if (f[j] != f[j]) s = __longlong_as_double(0x7ff8000000000000ll);  // only -inf and NaN seen so far
+      for (int u = 0; u < U; ++u) {
+        float f[V];
+        unpack16(r[u], f, x);
+#pragma unroll
+        for (int j = 0; j < V; ++j) cm = max_nan(cm, f[j]);
+      }
+      cm = warp_max_nan(cm);
+      if (!(cm <= mw)) {  // a larger (or NaN) max: rescale the sum so far (warp-uniform branch)
+        if (s != 0.0) s *= exp((double)mw - (double)cm);
+        mw = cm;
+      }
+      const ExpShift es(mw == -CUDART_INF_F ? 0.0f : mw);  // all -inf so far: exponentials are 0 against any value
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float f[V];
+        unpack16(r[u], f, x);
+        float2 acc = exp_pair(make_float2(f[0], f[1]), es);
+#pragma unroll
+        for (int j = 2; j < V; j += 2) acc = __fadd2_rn(acc, exp_pair(make_float2(f[j], f[j + 1]), es));
+        s += (double)(acc.x + acc.y);
       }
     }
-    // Block combine: the block max, then every thread rescales its sum to it.
-    const float bm = block_max(m, red);
-    s = (s != 0.0) ? s * exp((double)m - (double)bm) : 0.0;
-    s = block_sum(s, red_d);
-    if (threadIdx.x < csize) {
-      const unsigned pm = p ? peer_max[1] : peer_max[0];
-      const unsigned ps = p ? peer_sum[1] : peer_sum[0];
-      const unsigned pb = p ? peer_bar[1] : peer_bar[0];
-      st_async_u32(pm, __float_as_uint(bm), pb);
-      st_async_u64(ps, (unsigned long long)__double_as_longlong(s), pb);
+    s = warp_sum(s);
+    if (lane == 0) {
+      wmax[warp] = mw;
+      wsum[warp] = s;
     }
-    ok = mbar_wait(&bar_pair[p], (unsigned)(t >> 1) & 1u) && ok;
-    float M = xmax[p][0];
-    for (unsigned r = 1; r < csize; ++r) M = fmaxf(M, xmax[p][r]);
-    double total = 0.0;
-    for (unsigned r = 0; r < csize; ++r) {
-      const double sr = xsum[p][r];
-      if (sr != 0.0) total += sr * exp((double)xmax[p][r] - (double)M);
+    __syncthreads();
+
+    // Warp 0: this CTA's pair (a slice of -inf contributes m_c = -inf, s_c = 0), the exchange, the row's M and S.
+    // A NaN or +inf anywhere in the row, or a row of -inf, makes M or S NaN, so the row is all NaN.
+    if (warp == 0) {
+      const float ml = lane < kWarps ? wmax[lane] : -CUDART_INF_F;
+      const float mc = warp_max_nan(ml);
+      double sc = 0.0;
+      if (mc != -CUDART_INF_F) sc = warp_sum(lane < kWarps ? wsum[lane] * exp((double)ml - (double)mc) : 0.0);
+      if (t == 0) cluster_wait();
+      if (lane < (int)csize) {
+        st_async_u32(p ? peer_max[1] : peer_max[0], __float_as_uint(mc), p ? peer_bar[1] : peer_bar[0]);
+        st_async_u64(p ? peer_sum[1] : peer_sum[0], (unsigned long long)__double_as_longlong(sc),
+                     p ? peer_bar[1] : peer_bar[0]);
+      }
+      ok = mbar_wait(&bar_pair[p], (unsigned)(t >> 1) & 1u) && ok;
+      const float pm = lane < (int)csize ? xmax[p][lane] : -CUDART_INF_F;
+      const float M = warp_max_nan(pm);
+      const double S = warp_sum(lane < (int)csize ? xsum[p][lane] * exp((double)pm - (double)M) : 0.0);
+      if (lane == 0) {
+        row_m = M;
+        row_inv = (float)(1.0 / S);
+      }
     }
-    if (M == -CUDART_INF_F || M != M) total = __longlong_as_double(0x7ff8000000000000ll);  // all -inf / NaN row
-    const float inv = (float)(1.0 / total);
-    // Normalising pass (second read).
-    uint4* dst = reinterpret_cast<uint4*>(y + row * cols + beg);
-    for (long long i = threadIdx.x; i < nv; i += blockDim.x) {
-      float f[V];
-      unpack16(__ldg(src + i), f, x);
+    __syncthreads();
+
+    // Pass B: re-read (last use), exp(x - M) * inv, stream out.
+    const ExpShift es(row_m);
+    const float2 inv2 = make_float2(row_inv, row_inv);
+    uint4* dst = reinterpret_cast<uint4*>(y + row * cols);
+    for (long long i0 = vb + threadIdx.x; i0 < ve; i0 += kStep) {
+      uint4 r[U];
 #pragma unroll
-      for (int j = 0; j < V; ++j) f[j] = exp_shifted(f[j], M) * inv;
-      store16(reinterpret_cast<T*>(dst + i), f);
+      for (int u = 0; u < U; ++u) {
+        const long long i = i0 + (long long)u * kStreamThreads;
+        r[u] = i < ve ? __ldcs(src + i) : fill;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const long long i = i0 + (long long)u * kStreamThreads;
+        float f[V];
+        unpack16(r[u], f, x);
+#pragma unroll
+        for (int j = 0; j < V; j += 2) {
+          const float2 e = __fmul2_rn(exp_pair(make_float2(f[j], f[j + 1]), es), inv2);
+          f[j] = e.x;
+          f[j + 1] = e.y;
+        }
+        if (i < ve) store16(reinterpret_cast<T*>(dst + i), f);
+      }
     }
-    __syncthreads();  // red / red_d are reused by the next row
   }
   if (!ok) atomicOr(&g_softmax_status, CKB_STATUS_TIMEOUT);
-  (void)row_max;
 }
 
 // ----------------------------------------------------------------------------------------------- stream path ----
@@ -595,32 +750,34 @@ int start_cluster(const ClusterPlan& p, const T* x, T* y, long long rows, long l
   return (int)cudaGetLastError();
 }
 
-// Rows too long for shared-memory slices: clusters of 16 CTAs (8 if 16 cannot be resident), one row each (rows above
-// the grid's y limit loop).
+// Streaming cluster path: the smallest cluster (2..8) whose slices are at most 64 KB (8 for longer rows); one row per
+// cluster, rows above the grid's y limit loop.
 template <typename T>
-int start_cluster_wide(const T* x, T* y, long long rows, long long cols, cudaStream_t s) {
+int start_cluster_stream(const T* x, T* y, long long rows, long long cols, cudaStream_t s) {
   constexpr int V = VecN<T>::N;
-  auto kern = sm_cluster_wide<T>;
-  for (int cl = 16; cl >= 8; cl /= 2) {
-    if (cl > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
-      cudaGetLastError();
-      continue;
-    }
-    const long long slice = ((cols + cl - 1) / cl + V - 1) / V * V;
-    const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
-    cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = cluster_config(cl, 1, 0, s, attr);
-    int active = 0;
-    if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess || active <= 0) {
-      cudaGetLastError();
-      continue;
-    }
-    cfg.gridDim = dim3((unsigned)cl, gy, 1);
-    const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, x, y, rows, cols, slice);
-    if (err != cudaSuccess) return (int)err;
-    return (int)cudaGetLastError();
+  constexpr int U = V == 4 ? 8 : 4;
+  auto kern = sm_cluster_stream<T, U>;
+  const long long nvec = cols / V;
+  int cl = 2;
+  while (cl < kStreamMaxCluster && (nvec + cl - 1) / cl * 16 > 64 * 1024) cl *= 2;
+  if (cl > 8 && cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+    cudaGetLastError();
+    return -2;
   }
-  return -2;
+  const long long sv = (nvec + cl - 1) / cl;
+  const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = cluster_config(cl, 1, 0, s, attr);
+  cfg.blockDim = dim3(kStreamThreads, 1, 1);
+  int active = 0;
+  if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess || active <= 0) {
+    cudaGetLastError();
+    return -2;
+  }
+  cfg.gridDim = dim3((unsigned)cl, gy, 1);
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, x, y, rows, cols, sv);
+  if (err != cudaSuccess) return (int)err;
+  return (int)cudaGetLastError();
 }
 
 #ifndef CKB_SOFTMAX_BLOCK_MAX_THREADS
@@ -649,11 +806,11 @@ int dispatch(const T* x, T* y, long long rows, long long cols, cudaStream_t s) {
       return start_block<T, kMaxNV>(x, y, rows, c, threads, s);
     }
   }
-#ifndef CKB_SOFTMAX_FORCE_WIDE
-#define CKB_SOFTMAX_FORCE_WIDE 0
+#ifndef CKB_SOFTMAX_FORCE_STREAM
+#define CKB_SOFTMAX_FORCE_STREAM 0  // 1: every vectorised row of the cluster sizes takes the streaming cluster path
 #endif
-  if (vec && CKB_SOFTMAX_FORCE_WIDE) {
-    const int err = start_cluster_wide<T>(x, y, rows, cols, s);
+  if (vec && CKB_SOFTMAX_FORCE_STREAM) {
+    const int err = start_cluster_stream<T>(x, y, rows, cols, s);
     if (err != -2) return err;
   }
   if (vec) {
@@ -662,7 +819,7 @@ int dispatch(const T* x, T* y, long long rows, long long cols, cudaStream_t s) {
       const int err = start_cluster<T>(p, x, y, rows, cols, s);
       if (err != -2) return err;
     } else {
-      const int err = start_cluster_wide<T>(x, y, rows, cols, s);
+      const int err = start_cluster_stream<T>(x, y, rows, cols, s);
       if (err != -2) return err;
     }
   }
