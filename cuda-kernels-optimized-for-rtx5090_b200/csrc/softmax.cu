@@ -17,11 +17,11 @@
 //     read comes from L2);
 //   * stream path (unaligned pointers, cols not a multiple of the vector): one block per row reading the row three
 //     times (max, sum, normalise; the later reads mostly from L2).
-// Accuracy (fp32 outputs within 1e-6 relative of an fp64 softmax, elementwise): the group and block paths take
-// exp(x - max) with CUDA's expf on the fp32 difference and fold the difference's rounding error back in (TwoSum);
-// the cluster paths use exp_pair below (relative error within 2.1e-7, measured over every argument). Each thread sums
-// its exponentials pairwise per 16-byte vector into an fp64 accumulator, cross-thread and cross-CTA reductions run in
-// fp64, and the output is e * (float)(1 / sum) (or e * (float)(exp(m_c - M) / S) per cluster slice).
+// Accuracy (fp32 outputs within 1e-6 relative of an fp64 softmax, elementwise): every path takes exp(x - max) with
+// exp_pair below (relative error within 2.1e-7, measured over every argument; results below FLT_MIN flush to zero).
+// Each thread sums its exponentials pairwise per 16-byte vector into an fp64 accumulator, cross-thread and cross-CTA
+// reductions run in fp64, and the output is e * (float)(1 / sum) (or e * (float)(exp(m_c - M) / S) per cluster
+// slice). Maxima propagate NaN, so a row holding a NaN (or +inf, or only -inf) comes out all NaN, as in torch.
 #include "ckb200_softmax.h"
 #include "common.cuh"
 
@@ -44,19 +44,8 @@ __device__ __forceinline__ void store16(T* p, const float (&f)[VecN<T>::N]) {
   st_stream(p, pack16(f, p));
 }
 
-// exp(x - m) for m >= x. The fp32 difference d carries a rounding error of up to half an ulp of |d| (relative error
-// |d| * 2^-25 after exp, over 1e-6 once |d| > 32); TwoSum recovers that error lo exactly and exp(d + lo) is taken
-// as exp(d) * (1 + lo). A zero or NaN exponential (x = -inf, or an inf/NaN row) is left as it is.
-__device__ __forceinline__ float exp_shifted(float x, float m) {
-  const float d = x - m;
-  const float bv = d - x;
-  const float lo = (x - (d - bv)) + (-m - bv);
-  const float e = expf(d);
-  return e > 0.0f ? fmaf(e, lo, e) : e;
-}
-
 // ---------------------------------------------------------------------------------------------------------------
-// Packed exponentials for the cluster path: exp(x - M) for two values at a time on the fp32x2 pipe (sm_100).
+// Packed exponentials: exp(x - M) for two values at a time on the fp32x2 pipe (sm_100); every path uses them.
 // Method (from the mathematics; no library routine is restated): TwoSum (Knuth) splits x - M into s + lo exactly;
 // th = s * log2(e) rounded to fp32; E = 2^th by the ex2.approx instruction (flushes results below FLT_MIN to zero);
 // the residual r = (s + lo) - th * ln 2, with ln 2 as a float pair so that r is exact to far below an ulp of E and
@@ -110,18 +99,21 @@ __device__ __forceinline__ float2 exp_pair(float2 x, const ExpShift& e) {
   return __ffma2_rn(E, r, E);
 }
 
-// Pairwise sum of the values of one 16-byte vector.
-__device__ __forceinline__ float vec_sum(const float (&f)[4]) { return (f[0] + f[1]) + (f[2] + f[3]); }
-__device__ __forceinline__ float vec_sum(const float (&f)[8]) {
-  return ((f[0] + f[1]) + (f[2] + f[3])) + ((f[4] + f[5]) + (f[6] + f[7]));
-}
+// One value (the unaligned stream path): the pair routine with the value in both halves.
+__device__ __forceinline__ float exp_one(float x, const ExpShift& es) { return exp_pair(make_float2(x, x), es).x; }
 
-// In place: f = exp(f - m); returns their pairwise sum.
+// In place: f = exp(f - M) by pairs; returns their pairwise sum.
 template <int V>
-__device__ __forceinline__ float exp_vec(float (&f)[V], float m) {
+__device__ __forceinline__ float exp_vec2(float (&f)[V], const ExpShift& es) {
+  float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
-  for (int j = 0; j < V; ++j) f[j] = exp_shifted(f[j], m);
-  return vec_sum(f);
+  for (int j = 0; j < V; j += 2) {
+    const float2 e = exp_pair(make_float2(f[j], f[j + 1]), es);
+    f[j] = e.x;
+    f[j + 1] = e.y;
+    acc = j == 0 ? e : __fadd2_rn(acc, e);
+  }
+  return acc.x + acc.y;
 }
 
 // ------------------------------------------------------------------------------------------------ group path ----
@@ -151,13 +143,14 @@ __global__ void __launch_bounds__(256) sm_group(const T* __restrict__ x, T* __re
   for (int k = 0; k < NV; ++k)
     if (in[k]) {
 #pragma unroll
-      for (int j = 0; j < V; ++j) m = fmaxf(m, v[k][j]);
+      for (int j = 0; j < V; ++j) m = max_nan(m, v[k][j]);
     }
-  m = warp_max<G>(m);
+  m = warp_max_nan<G>(m);
+  const ExpShift es(m);
   double s = 0.0;
 #pragma unroll
   for (int k = 0; k < NV; ++k)
-    if (in[k]) s += (double)exp_vec(v[k], m);
+    if (in[k]) s += (double)exp_vec2(v[k], es);
   s = warp_sum<G>(s);
   const float inv = (float)(1.0 / s);
 #pragma unroll
@@ -194,22 +187,21 @@ __global__ void __launch_bounds__(MAXT) sm_block(const T* __restrict__ x, T* __r
   for (int k = 0; k < NV; ++k)
     if (in[k]) {
 #pragma unroll
-      for (int j = 0; j < V; ++j) m = fmaxf(m, v[k][j]);
+      for (int j = 0; j < V; ++j) m = max_nan(m, v[k][j]);
     }
-  m = warp_max(m);
+  m = warp_max_nan(m);
   if (lane == 0) red_m[warp] = m;
   __syncthreads();
-  m = red_m[0];
-  for (int i = 1; i < warps; ++i) m = fmaxf(m, red_m[i]);
+  m = warp_max_nan(lane < warps ? red_m[lane] : -CUDART_INF_F);
+  const ExpShift es(m);
   double s = 0.0;
 #pragma unroll
   for (int k = 0; k < NV; ++k)
-    if (in[k]) s += (double)exp_vec(v[k], m);
+    if (in[k]) s += (double)exp_vec2(v[k], es);
   s = warp_sum(s);
   if (lane == 0) red_s[warp] = s;
   __syncthreads();
-  s = 0.0;
-  for (int i = 0; i < warps; ++i) s += red_s[i];
+  s = warp_sum(lane < warps ? red_s[lane] : 0.0);
   const float inv = (float)(1.0 / s);
 #pragma unroll
   for (int k = 0; k < NV; ++k)
@@ -229,14 +221,15 @@ constexpr int kMaxStages = 4;
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
-// Block-wide max / sum of one value per thread through `red` (32 slots); every thread gets the same result.
+// Block-wide max (NaN-propagating) / sum of one value per thread through `red` (32 slots); every thread gets the same
+// result.
 __device__ __forceinline__ float block_max(float v, float* red) {
-  v = warp_max(v);
+  v = warp_max_nan(v);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
   const int warps = blockDim.x >> 5;
   float r = red[0];
-  for (int i = 1; i < warps; ++i) r = fmaxf(r, red[i]);
+  for (int i = 1; i < warps; ++i) r = max_nan(r, red[i]);
   return r;
 }
 __device__ __forceinline__ double block_sum(double v, double* red) {
@@ -612,13 +605,13 @@ __global__ void __launch_bounds__(1024) sm_stream(const T* __restrict__ x, T* __
   const T* xr = x + (long long)blockIdx.x * cols;
   T* yr = y + (long long)blockIdx.x * cols;
   float m = -CUDART_INF_F;
-  for (long long i = threadIdx.x; i < cols; i += blockDim.x) m = fmaxf(m, to_f32(xr[i]));
-  m = block_max(m, red);
+  for (long long i = threadIdx.x; i < cols; i += blockDim.x) m = max_nan(m, to_f32(xr[i]));
+  const ExpShift es(block_max(m, red));
   double s = 0.0;
-  for (long long i = threadIdx.x; i < cols; i += blockDim.x) s += (double)exp_shifted(to_f32(xr[i]), m);
+  for (long long i = threadIdx.x; i < cols; i += blockDim.x) s += (double)exp_one(to_f32(xr[i]), es);
   s = block_sum(s, red_d);
   const float inv = (float)(1.0 / s);
-  for (long long i = threadIdx.x; i < cols; i += blockDim.x) yr[i] = from_f32<T>(exp_shifted(to_f32(xr[i]), m) * inv);
+  for (long long i = threadIdx.x; i < cols; i += blockDim.x) yr[i] = from_f32<T>(exp_one(to_f32(xr[i]), es) * inv);
 }
 
 // ------------------------------------------------------------------------------------------------- dispatch -----

@@ -106,3 +106,21 @@ def test_matches_reference_kernel():
         assert_rel(got, want, REL, "ours")
         # the reference kernel against the same oracle, for the record (its division-based path is as accurate)
         assert_rel(ref, want, 2 * REL, "reference kernel")
+
+
+@pytest.mark.parametrize("cols", [128, 8192, 262144, 4194304, 1001])
+def test_wide_dynamic_range(cols):
+    """Rows spanning 0 .. -120 below their max (every path: group, block, cluster, streaming cluster, stream):
+    outputs of at least FLT_MIN keep 1e-6 relative; smaller true values come out as 0 or at most FLT_MIN (the
+    exponential flushes results below FLT_MIN)."""
+    g = torch.Generator().manual_seed(cols)
+    x = -torch.rand(3, cols, generator=g) * 120.0
+    x[:, 0] = 0.0
+    y = softmax.softmax(x.cuda()).cpu().double().numpy()
+    want = orc.softmax_f64(x).numpy()
+    tiny = np.finfo(np.float32).tiny
+    normal = want >= tiny
+    err = np.abs(y[normal] - want[normal]) / want[normal]
+    assert err.max() <= REL, f"{cols}: worst {err.max():.3e}"
+    assert (np.abs(y[~normal]) <= tiny).all()
+    assert normal.sum() > 0 and (~normal).sum() > 0
