@@ -327,37 +327,35 @@ def time_case(case, steps, warmup, world, sampler_gpu=None):
     return max_over_ranks(ms, world), (sampler.summary() if sampler else None)
 
 
-def e2e_rmsnorm(steps, warmup, world):
-    """Public API end to end: pinned host x -> device, ckb200.rmsnorm.rmsnorm, device y -> pinned host."""
-    from ckb200 import rmsnorm, workloads
+def e2e_rmsnorm(steps, warmup, world, chunks=8):
+    """Public API end to end: pinned host x -> device -> ckb200.rmsnorm.rmsnorm -> pinned host y, every step moving
+    the whole batch in and out, through ckb200.hostpipe.RowPipeline (row chunks on copy-in / compute / copy-out
+    streams, so the two copy directions and the kernels overlap)."""
+    from ckb200 import hostpipe, rmsnorm, workloads
 
     base = workloads.rmsnorm_16384x4096()
     hx = base["x"].pin_memory()
     hy = torch.empty_like(hx).pin_memory()
     w = base["weight"].cuda()
-    dx = torch.empty_like(hx, device="cuda")
-    dy = torch.empty_like(dx)
-
-    def step():
-        dx.copy_(hx, non_blocking=True)
-        rmsnorm.rmsnorm(dx, w, out=dy)
-        hy.copy_(dy, non_blocking=True)
+    rows, cols = hx.shape
+    pipe = hostpipe.RowPipeline(lambda x, y: rmsnorm.rmsnorm(x, w, out=y), rows, cols, hx.dtype, chunks=chunks)
 
     for _ in range(warmup):
-        step()
-    torch.cuda.synchronize()
+        pipe(hx, hy)
+    pipe.synchronize()
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
+    pipe.record_start(start)
     for _ in range(steps):
-        step()
-    end.record()
-    torch.cuda.synchronize()
+        pipe(hx, hy)
+    pipe.record_end(end)
+    end.synchronize()
     ms = max_over_ranks(start.elapsed_time(end), world)
     nbytes = workloads.ALGORITHMIC_BYTES[HEADLINE]
     return {"value": round(world * nbytes * steps / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": hx.numel() * hx.element_size(),
-            "d2h_bytes_per_step": hy.numel() * hy.element_size(), "ms_per_step": round(ms / steps, 4)}
+            "d2h_bytes_per_step": hy.numel() * hy.element_size(), "ms_per_step": round(ms / steps, 4),
+            "pipeline": f"{len(pipe.bounds)} row chunks, copy-in / compute / copy-out streams"}
 
 
 # --------------------------------------------------------------------------------------------- CPU baselines ----

@@ -74,3 +74,12 @@ def test_rope_inv_freq_is_the_cache_builders():
     cos, sin = cos_sin_cache(10000.0, 128, 4096)
     ang = (torch.arange(4096).float()[:, None] * f[None, :])
     assert torch.equal(torch.cat([ang, ang], -1).cos(), cos)
+
+
+def test_row_pipeline_rejects_empty_shapes_before_touching_the_gpu():
+    from ckb200 import hostpipe
+
+    with pytest.raises(ValueError, match="shape"):
+        hostpipe.RowPipeline(lambda a, b: None, 0, 8, torch.float32)
+    with pytest.raises(ValueError, match="chunks"):
+        hostpipe.RowPipeline(lambda a, b: None, 4, 8, torch.float32, chunks=0)
