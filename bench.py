@@ -434,6 +434,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     ap.add_argument("--sweep-steps", type=int, default=300)
     ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--vocab-exchange", choices=("peer", "nccl"), default="peer",
+                    help="topk_vocab workload: the fused peer-memory exchange or an NCCL all-gather")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -484,7 +486,8 @@ def main():
 
 def run_vocab(args, rank, world, local):
     """Vocab-sharded top-k (strong scaling): the [512, 151936] fp32 logits split by columns over the ranks; a step is
-    the local top-50 kernel, one NCCL all-gather of the [512, 50] composite lists and the merge kernel."""
+    the local top-50 kernel, the exchange of the [512, 50] composite lists (by default fused into the kernels over
+    peer memory; --vocab-exchange nccl: one NCCL all-gather) and the merge kernel."""
     from ckb200 import sharded, workloads
 
     peak, peak_kind = hbm_peak()
@@ -492,7 +495,8 @@ def run_vocab(args, rank, world, local):
     full = workloads.topk_512x151936()["x"]
     lo, hi = sharded.col_range(full.shape[1], rank, world)
     shards = [full[:, lo:hi].contiguous().to(dev) for _ in range(2)]  # two copies: rotate past L2
-    op = sharded.VocabShardedTopK(full.shape[0], 50, device=dev)
+    peer = args.vocab_exchange == "peer"
+    op = (sharded.PeerVocabShardedTopK if peer else sharded.VocabShardedTopK)(full.shape[0], 50, device=dev)
     for i in range(args.warmup):
         op(shards[i % 2], lo)
     torch.cuda.synchronize()
@@ -518,12 +522,17 @@ def run_vocab(args, rank, world, local):
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
                 "data": "synthetic (seeded, BASELINE config distributions)",
                 "config": {"workload": args.workload, "cols_per_gpu": hi - lo, "parallelism": f"vocab-sharded x{world}",
-                           "collective": "NCCL all_gather_into_tensor of [512, 50] int64 composites"},
+                           "collective": ("fused: the shard kernel stores its [512, 50] composite lists into every "
+                                          "rank's memory over NVLink (CUDA IPC) and raises per-row flags; the merge "
+                                          "kernel waits on them" if peer else
+                                          "NCCL all_gather_into_tensor of [512, 50] int64 composites")},
                 "rows_per_s": round(512 * args.steps / (ms * 1e-3), 1),
                 "roofline": {"bound": "hbm", "achieved": round(nbytes / world / (ms / args.steps * 1e-3) / 1e9, 1),
                              "peak": peak, "unit": "GB/s per GPU", "peak_kind": peak_kind},
                 "clocks": sampler.summary(), "gpu_launches": 2 * args.steps, "check": ok}
         print(json.dumps(line), flush=True)
+    if peer:
+        op.close()
     if world > 1:
         dist.destroy_process_group()
 

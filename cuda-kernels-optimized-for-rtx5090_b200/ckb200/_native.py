@@ -13,6 +13,7 @@ import torch
 from . import build as _build
 
 _VP, _LL, _INT, _FLT = ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_float
+_UINT, _PVP = ctypes.c_uint, ctypes.POINTER(ctypes.c_void_p)
 
 # Symbol -> (restype, argtypes), per op; mirrors include/ckb200_<op>.h.
 SIGNATURES = {
@@ -34,6 +35,14 @@ SIGNATURES = {
         "ckb_topk_shard_launch": (_INT, [_VP] * 4 + [_LL, _LL, _LL, _INT, _INT, _LL, _VP]),
         "ckb_topk_merge_launch": (_INT, [_VP, _INT, _VP, _VP, _LL, _INT, _INT, _VP]),
         "ckb_topk_launch_noalloc": (_INT, [_VP, _VP, _VP, _LL, _LL, _INT, _INT, _VP]),
+        "ckb_topk_shard_push_launch": (_INT, [_VP, _VP, _VP, _LL, _LL, _LL, _INT, _INT, _LL, _PVP, _PVP, _INT, _INT,
+                                              _UINT, _VP]),
+        "ckb_topk_merge_wait_launch": (_INT, [_VP, _VP, _INT, _UINT, _VP, _VP, _LL, _INT, _INT, _VP]),
+        "ckb_p2p_alloc": (_INT, [_PVP, ctypes.c_ulonglong]),
+        "ckb_p2p_free": (_INT, [_VP]),
+        "ckb_p2p_export": (_INT, [_VP, _VP]),
+        "ckb_p2p_import": (_INT, [_VP, _PVP]),
+        "ckb_p2p_close": (_INT, [_VP]),
         "ckb_topk_status": (_INT, [_INT]),
     },
 }

@@ -8,12 +8,18 @@ partitionings its row-wise ops admit:
     rank selects its local top k as sorted 64-bit composites carrying global column indices, an all-gather brings
     every rank's [rows, k] list to every rank ([world, rows, k], world * rows * k * 8 bytes), and the merge kernel
     ranks them into the final top k. Composites are distinct, so the merge is exact and ties still go to the lower
-    global index.
+    global index. PeerVocabShardedTopK does the same exchange without a collective call: the shard kernel stores
+    its lists straight into every rank's memory over NVLink (CUDA IPC mappings) and raises per-row flags there, and
+    the merge kernel waits on those flags.
 """
+
+import ctypes
+
 
 import torch
 import torch.distributed as dist
 
+from . import _native
 from . import topk as _topk
 
 
@@ -70,3 +76,93 @@ class VocabShardedTopK:
         else:
             dist.all_gather(list(self.gathered.unbind(0)), self.lists, group=self.group)
         return _topk.merge_lists(self.gathered, x_shard.dtype, self.k)
+
+
+def exchange_layout(world, rows, k):
+    """Byte layout of one parity half of a rank's exchange buffer: (half_bytes, lists_offset, flags_offset) for
+    lists [world][rows][k] uint64 then flags [world][rows] uint32, the half padded to 256 bytes."""
+    lists_bytes = world * rows * k * 8
+    flags_bytes = world * rows * 4
+    half = (lists_bytes + flags_bytes + 255) // 256 * 256
+    return half, 0, lists_bytes
+
+
+def next_epoch(epoch):
+    """The epoch after `epoch` (32-bit, never 0, parity always alternating: 0xffffffff is followed by 2)."""
+    e = epoch + 1
+    return e if e <= 0xFFFFFFFF else 2
+
+
+class PeerVocabShardedTopK:
+    """The vocab-sharded top-k with its all-gather done by the kernels over peer memory.
+
+    Every rank allocates one exchange buffer (two parity halves, exchange_layout) through the top-k library, and the
+    ranks swap CUDA IPC handles once (a host all-gather of 64-byte handles), so each holds every rank's buffer
+    address. A call with epoch e (counted from 1) uses half e & 1: ckb_topk_shard_push_launch stores this rank's
+    row lists into slot `rank` of every rank's half and sets the row flags to e there, then
+    ckb_topk_merge_wait_launch waits on this rank's own flags and merges. Two halves suffice: a rank starts call
+    e + 2 only after its merge of call e + 1 saw every rank's lists of e + 1, which those ranks pushed after
+    finishing their merges of call e. Call close() on every rank (it synchronises them) before the process group
+    goes."""
+
+    def __init__(self, rows, k=_topk.K, device=None, group=None):
+        self.group = group
+        self.rows, self.k = rows, k
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        distributed = dist.is_initialized()
+        self.world = dist.get_world_size(group) if distributed else 1
+        self.rank = dist.get_rank(group) if distributed else 0
+        if self.world > 8:
+            raise ValueError(f"PeerVocabShardedTopK: at most 8 ranks, got {self.world}")
+        self.half, self.lists_off, self.flags_off = exchange_layout(self.world, rows, k)
+        lib = _native.load("topk")
+        self._lib = lib
+        own = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _native.check(lib.ckb_p2p_alloc(ctypes.byref(own), 2 * self.half))
+            handle = ctypes.create_string_buffer(64)
+            _native.check(lib.ckb_p2p_export(own, handle))
+        self._own = own.value
+        handles = [handle.raw]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, handle.raw, group=group)
+        self.bases, self._imported = [], []
+        with torch.cuda.device(self.device):
+            for p in range(self.world):
+                if p == self.rank:
+                    self.bases.append(self._own)
+                    continue
+                ptr = ctypes.c_void_p()
+                _native.check(lib.ckb_p2p_import(ctypes.create_string_buffer(handles[p], 64), ctypes.byref(ptr)))
+                self.bases.append(ptr.value)
+                self._imported.append(ptr.value)
+        self.epoch = 0
+
+    def __call__(self, x_shard, col_offset):
+        """(values, int64 indices) [rows, k] of the full rows; x_shard [rows, local_cols] holds global columns
+        [col_offset, col_offset + local_cols). Launches two kernels on the current stream, no collective call."""
+        if x_shard.shape[0] != self.rows:
+            raise ValueError(f"PeerVocabShardedTopK: {x_shard.shape[0]} rows, built for {self.rows}")
+        self.epoch = next_epoch(self.epoch)
+        par = (self.epoch & 1) * self.half
+        lists = [b + par + self.lists_off for b in self.bases]
+        flags = [b + par + self.flags_off for b in self.bases]
+        _topk.shard_push(x_shard, col_offset, self.k, lists, flags, self.rank, self.epoch)
+        return _topk.merge_wait(lists[self.rank], flags[self.rank], self.world, self.epoch, self.rows, self.k,
+                                x_shard.dtype, x_shard.device)
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's once every rank is done with them."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for ptr in self._imported:
+                self._lib.ckb_p2p_close(ctypes.c_void_p(ptr))
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            self._lib.ckb_p2p_free(ctypes.c_void_p(self._own))
+        self._own, self._imported, self.bases = None, [], []

@@ -131,3 +131,41 @@ def merge_lists(lists, dtype, k=K):
                                         _DTYPES[dtype], _native.stream_of(lists))
     _native.check(err)
     return values, indices
+
+
+def shard_push(x, col_offset, k, lists_ptrs, flags_ptrs, rank, epoch):
+    """Local half of the vocab-sharded top-k over peer memory: the shard's row lists go to slot `rank` of every
+    rank's exchange buffer (lists_ptrs / flags_ptrs: one device address per rank, this call's parity) and each row's
+    flag is set to `epoch` there (ckb_topk_shard_push_launch)."""
+    import ctypes
+
+    dtype = _check_x(x, k)
+    x = x.contiguous()
+    rows, cols = x.shape
+    chunk, work = _plan(x, rows, cols, dtype, k)
+    counters = _row_counters(x.device, rows)
+    world = len(lists_ptrs)
+    lists_arr = (ctypes.c_void_p * world)(*lists_ptrs)
+    flags_arr = (ctypes.c_void_p * world)(*flags_ptrs)
+    lib = _native.load("topk")
+    with torch.cuda.device(x.device):
+        err = lib.ckb_topk_shard_push_launch(x.data_ptr(), work.data_ptr(), counters.data_ptr(), rows, cols,
+                                             int(col_offset), k, dtype, chunk, lists_arr, flags_arr, world, rank,
+                                             epoch, _native.stream_of(x))
+    _native.check(err)
+
+
+def merge_wait(lists_ptr, flags_ptr, world, epoch, rows, k, dtype, device, values=None, indices=None):
+    """Merge half over peer memory (ckb_topk_merge_wait_launch): waits per row for every rank's list of this epoch
+    in this rank's exchange buffer, then (values in dtype, int64 indices) [rows, k]."""
+    if dtype not in _DTYPES:
+        raise ValueError(f"topk merge: dtype {dtype}")
+    values = torch.empty((rows, k), dtype=dtype, device=device) if values is None else values
+    indices = torch.empty((rows, k), dtype=torch.int64, device=device) if indices is None else indices
+    lib = _native.load("topk")
+    with torch.cuda.device(device):
+        err = lib.ckb_topk_merge_wait_launch(lists_ptr, flags_ptr, world, epoch, values.data_ptr(),
+                                             indices.data_ptr(), rows, k, _DTYPES[dtype],
+                                             torch.cuda.current_stream(device).cuda_stream)
+    _native.check(err)
+    return values, indices

@@ -30,6 +30,7 @@
 #include <math_constants.h>
 
 #include <climits>
+#include <cstring>
 
 namespace ckb {
 
@@ -556,6 +557,19 @@ __device__ __forceinline__ u64 raise_bound(u64 lo, u64 kth) {
   return b > lo ? b : lo;
 }
 
+constexpr int kMaxPeers = 8;
+
+// Mode 2 (vocab-sharded top-k over peer memory): each rank's exchange buffer holds, for the current call's parity,
+// lists [world][rows][k] and flags [world][rows]; this rank writes its row lists into slot `rank` of every rank's
+// buffer and then sets flag [rank][row] = epoch there.
+struct PushArgs {
+  u64* lists[kMaxPeers];        // every rank's lists base for this parity (this rank's own included)
+  unsigned* flags[kMaxPeers];   // every rank's flags base for this parity
+  int world, rank;
+  unsigned epoch;
+  long long rows;
+};
+
 struct SegArgs {
   const void* x;
   void* values;          // mode 0: [rows, k] in x's dtype
@@ -565,7 +579,17 @@ struct SegArgs {
   unsigned* counters;    // [rows], zero on entry, left zero
   long long col_offset;  // added to every column index
   int cols, k, mode;
+  PushArgs push;         // mode 2
 };
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 // Writes entry j of the row's final top k in the requested form.
 template <typename T>
@@ -573,9 +597,20 @@ __device__ __forceinline__ void emit(const SegArgs& a, long long row, int j, u64
   if (a.mode == 0) {
     reinterpret_cast<T*>(a.values)[row * a.k + j] = decode_value<T>(c);
     a.indices[row * a.k + j] = decode_index(c);
-  } else {
+  } else if (a.mode == 1) {
     a.lists[row * a.k + j] = c;
+  } else {
+    const long long at = ((long long)a.push.rank * a.push.rows + row) * a.k + j;
+    for (int p = 0; p < a.push.world; ++p) a.push.lists[p][at] = c;  // NVLink stores to every rank (and itself)
   }
+}
+
+// Mode 2, after every emit of the row: the writers' stores are made visible system-wide before the row's flag moves
+// on each rank (the block barrier orders every writer's fence before the flag stores).
+__device__ __forceinline__ void publish_row(const SegArgs& a, long long row, int tid) {
+  __threadfence_system();
+  __syncthreads();
+  if (tid < a.push.world) st_release_sys(a.push.flags[tid] + (long long)a.push.rank * a.push.rows + row, a.push.epoch);
 }
 
 // Grid (nseg, rows). A row's 16-byte aligned body is split evenly into nseg segments of vectors; the elements before
@@ -847,6 +882,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   // Output, or the multi-segment merge by the row's last CTA.
   if (nseg == 1) {
     for (int i = tid; i < k; i += kThreads) emit<T>(a, row, i, cand[i]);
+    if (a.mode == 2) publish_row(a, row, tid);
     return;
   }
   u64* wr = a.work + ((long long)row * nseg + seg) * k;
@@ -883,6 +919,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   }
   for (int i = tid; i < k; i += kThreads) emit<T>(a, row, i, la[i]);
   if (tid == 0) a.counters[row] = 0u;
+  if (a.mode == 2) publish_row(a, row, tid);
 }
 
 // Merge of nlists sorted composite lists per row, lists laid out [nlists][rows][k] (an all-gather's output); one
@@ -904,6 +941,54 @@ __global__ void __launch_bounds__(256) topk_merge(const u64* __restrict__ lists,
     const int own = i / k;
     int rank = i - own * k;
     for (int l = 0; l < nlists && rank < k; ++l)
+      if (l != own) rank += count_greater(sl + l * k, k, c);
+    if (rank < k) {
+      values[row * k + rank] = decode_value<T>(c);
+      indices[row * k + rank] = decode_index(c);
+    }
+  }
+}
+
+// Merge of the vocab-sharded variant over peer memory: lists [world][rows][k] and flags [world][rows] in this rank's
+// exchange buffer (this call's parity). Thread p < world of row `row`'s CTA waits (bounded) until rank p has
+// published the row for this epoch; the lists are then read through L2 (peers wrote them during this kernel's life,
+// so not through the read-only path) and ranked as in topk_merge. A wait that runs out sets the status word.
+template <typename T>
+__global__ void __launch_bounds__(256) topk_merge_wait(const u64* lists, const unsigned* flags, int world,
+                                                       unsigned epoch, long long rows, int k, T* __restrict__ values,
+                                                       long long* __restrict__ indices) {
+  extern __shared__ __align__(16) u64 sl[];
+  __shared__ int s_timeout;
+  const long long row = blockIdx.x;
+  if (threadIdx.x == 0) s_timeout = 0;
+  __syncthreads();
+  if (threadIdx.x < world) {
+    const unsigned* f = flags + (long long)threadIdx.x * rows + row;
+    if ((int)(ld_acquire_sys(f) - epoch) < 0) {
+      const unsigned long long start = global_ns();
+      while ((int)(ld_acquire_sys(f) - epoch) < 0) {
+        if (global_ns() - start > kWaitLimitNs) {
+          s_timeout = 1;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  __syncthreads();
+  if (s_timeout && threadIdx.x == 0) atomicOr(&g_topk_status, CKB_STATUS_TIMEOUT);
+  const int total = world * k;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int l = i / k, j = i - l * k;
+    sl[i] = __ldcg(lists + ((long long)l * rows + row) * k + j);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const u64 c = sl[i];
+    if (c == 0ull) continue;
+    const int own = i / k;
+    int rank = i - own * k;
+    for (int l = 0; l < world && rank < k; ++l)
       if (l != own) rank += count_greater(sl + l * k, k, c);
     if (rank < k) {
       values[row * k + rank] = decode_value<T>(c);
@@ -1055,6 +1140,94 @@ CKB_EXPORT int ckb_topk_merge_launch(const unsigned long long* lists, int nlists
   }
   return (int)cudaGetLastError();
 }
+
+// Vocab-sharded variant over peer memory, local half (no counterpart in the reference): as ckb_topk_shard_launch,
+// but each row's sorted list goes to slot `rank` of every rank's exchange buffer (lists[p] + (rank * rows + row) * k
+// for p < world, NVLink stores) and flags[p][rank * rows + row] is then set to `epoch` (release, system scope).
+// lists / flags are host arrays of `world` device pointers (this call's parity of each rank's buffer, this rank's
+// own included). 1 <= world <= 8, 0 <= rank < world, epoch != 0.
+CKB_EXPORT int ckb_topk_shard_push_launch(const void* x, void* work, void* counters, long long rows, long long cols,
+                                          long long col_offset, int k, int dtype, long long chunk,
+                                          unsigned long long* const* lists, unsigned* const* flags, int world,
+                                          int rank, unsigned epoch, cudaStream_t stream) {
+  if (rows <= 0 || k <= 0) return 0;
+  if (dtype != kF32 && dtype != kBF16) return -1;
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || epoch == 0u || !lists || !flags) return -1;
+  const int elem = dtype == kBF16 ? 2 : 4;
+  if (col_offset < 0 || col_offset + cols > INT_MAX / 2 || bad_args(x, rows, cols, k, chunk, elem)) return -1;
+  if (chunk > cols) chunk = cols;
+  SegArgs a{x, nullptr, nullptr, nullptr, (u64*)work, (unsigned*)counters, col_offset, (int)cols, k, 2, {}};
+  for (int p = 0; p < world; ++p) {
+    if (!lists[p] || !flags[p]) return -1;
+    a.push.lists[p] = (u64*)lists[p];
+    a.push.flags[p] = flags[p];
+  }
+  a.push.world = world;
+  a.push.rank = rank;
+  a.push.epoch = epoch;
+  a.push.rows = rows;
+  if (dtype == kF32) return start_seg<float>(a, rows, segments(cols, chunk), stream);
+  return start_seg<__nv_bfloat16>(a, rows, segments(cols, chunk), stream);
+}
+
+// Vocab-sharded variant over peer memory, merge half (no counterpart in the reference): lists [world][rows][k] and
+// flags [world][rows] are this rank's exchange buffer (this call's parity). Each row waits until every rank has
+// published it for `epoch` (at most 2 s; then the status word records the timeout and the row is merged from
+// whatever is there), then values [rows, k] (dtype 0 / 1) and int64 indices [rows, k] as ckb_topk_merge_launch.
+CKB_EXPORT int ckb_topk_merge_wait_launch(const unsigned long long* lists, const unsigned* flags, int world,
+                                          unsigned epoch, void* values, void* indices, long long rows, int k,
+                                          int dtype, cudaStream_t stream) {
+  if (rows <= 0 || k <= 0) return 0;
+  if (world < 1 || world > kMaxPeers || epoch == 0u || k > kMaxK || rows > INT_MAX || !lists || !flags) return -1;
+  const int smem = world * k * 8;
+  if (dtype == kF32) {
+    if (cudaFuncSetAttribute(topk_merge_wait<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return (int)cudaGetLastError();
+    topk_merge_wait<float><<<(unsigned)rows, 256, (size_t)smem, stream>>>((const u64*)lists, flags, world, epoch,
+                                                                          rows, k, (float*)values,
+                                                                          (long long*)indices);
+  } else if (dtype == kBF16) {
+    if (cudaFuncSetAttribute(topk_merge_wait<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return (int)cudaGetLastError();
+    topk_merge_wait<__nv_bfloat16><<<(unsigned)rows, 256, (size_t)smem, stream>>>(
+        (const u64*)lists, flags, world, epoch, rows, k, (__nv_bfloat16*)values, (long long*)indices);
+  } else {
+    return -1;
+  }
+  return (int)cudaGetLastError();
+}
+
+// Exchange buffers for the peer-memory variant: device memory of `bytes` (zeroed) that other processes can map
+// through a 64-byte CUDA IPC handle. alloc/free on the owning process; export gives the handle of an alloc'd base
+// pointer; import maps a peer's handle (peer access enabled lazily) and close unmaps it. Each returns 0 or the
+// cudaError_t.
+CKB_EXPORT int ckb_p2p_alloc(void** ptr, unsigned long long bytes) {
+  if (!ptr || bytes == 0) return -1;
+  cudaError_t e = cudaMalloc(ptr, (size_t)bytes);
+  if (e != cudaSuccess) return (int)e;
+  e = cudaMemset(*ptr, 0, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  return (int)e;
+}
+CKB_EXPORT int ckb_p2p_free(void* ptr) { return (int)cudaFree(ptr); }
+CKB_EXPORT int ckb_p2p_export(const void* ptr, void* handle) {
+  if (!ptr || !handle) return -1;
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return (int)e;
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  memcpy(handle, &h, sizeof(h));
+  return 0;
+}
+CKB_EXPORT int ckb_p2p_import(const void* handle, void** ptr) {
+  if (!handle || !ptr) return -1;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return (int)cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+}
+CKB_EXPORT int ckb_p2p_close(void* ptr) { return (int)cudaIpcCloseMemHandle(ptr); }
 
 // Status word of this library's kernels since the last reset (0 = fine). The streaming kernel waits only on its own
 // asynchronous copies, which always complete, so nothing sets it today; the entry point stays for callers that poll

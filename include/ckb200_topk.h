@@ -33,6 +33,35 @@ int ckb_topk_shard_launch(const void* x, unsigned long long* lists, void* work, 
 int ckb_topk_merge_launch(const unsigned long long* lists, int nlists, void* values, void* indices, long long rows,
                           int k, int dtype, cudaStream_t stream);
 
+/* Vocab-sharded variant over peer memory (one process per GPU; no counterpart in the reference, which is single-GPU).
+ * Each rank owns an exchange buffer that every rank maps (ckb_p2p_*), double buffered by call parity; a parity half
+ * holds lists [world][rows][k] (uint64 composites) and flags [world][rows] (uint32, zero at allocation).
+ * Local half: as ckb_topk_shard_launch, but every row's sorted list is stored into slot `rank` of every rank's lists
+ * (NVLink stores) and then flags[p][rank * rows + row] = epoch on every rank p (release, system scope). lists / flags:
+ * host arrays of `world` device pointers to this parity's half of each rank's buffer (this rank's own included).
+ * 1 <= world <= 8, 0 <= rank < world, epoch != 0 (callers count calls from 1; parity = epoch & 1). */
+int ckb_topk_shard_push_launch(const void* x, void* work, void* counters, long long rows, long long cols,
+                               long long col_offset, int k, int dtype, long long chunk,
+                               unsigned long long* const* lists, unsigned* const* flags, int world, int rank,
+                               unsigned epoch, cudaStream_t stream);
+
+/* Merge half: lists / flags = this rank's own buffer half for this parity. Row r waits until flags[p][r] reaches
+ * `epoch` for every rank p (at most 2 s; a wait that runs out sets ckb_topk_status() and the row is merged from
+ * whatever is there), then writes values [rows, k] (dtype 0 fp32 / 1 bf16) and int64 indices [rows, k] as
+ * ckb_topk_merge_launch. */
+int ckb_topk_merge_wait_launch(const unsigned long long* lists, const unsigned* flags, int world, unsigned epoch,
+                               void* values, void* indices, long long rows, int k, int dtype, cudaStream_t stream);
+
+/* Exchange buffers: alloc gives `bytes` of zeroed device memory on the current device; export writes the 64-byte CUDA
+ * IPC handle of an alloc'd pointer; import maps a peer's handle into this process (peer access enabled lazily);
+ * close unmaps an imported pointer; free releases an alloc'd one. Each returns 0 or the cudaError_t (-1 for null
+ * arguments). */
+int ckb_p2p_alloc(void** ptr, unsigned long long bytes);
+int ckb_p2p_free(void* ptr);
+int ckb_p2p_export(const void* ptr, void* handle);
+int ckb_p2p_import(const void* handle, void** ptr);
+int ckb_p2p_close(void* ptr);
+
 /* The top-k of launch() for callers that cannot allocate device memory (a host framework that owns the GPU's memory
  * through its own fixed-budget allocator, or a path that cannot afford cudaMalloc's device synchronisation): no
  * workspace or counters are passed; a 4 MiB scratch array compiled into this library (held on every GPU that loads

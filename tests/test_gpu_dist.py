@@ -1,6 +1,7 @@
 """Multi-GPU paths over NCCL with one process per GPU (skipped with fewer than 2 GPUs):
   * the vocab-sharded top-k (local shard kernel -> all_gather_into_tensor -> merge kernel) gives every rank the
-    single-GPU answer, bit for bit;
+    single-GPU answer, bit for bit, and so does its peer-memory form (PeerVocabShardedTopK: NVLink stores and
+    per-row flags instead of the collective), call after call (both parity halves, fp32 and bf16);
   * row sharding: each rank normalises its own rows; gathered, they equal the oracle.
 Ranks are spawned processes with a short process-group timeout, so a stuck collective ends the test with an error."""
 
@@ -49,6 +50,15 @@ def _worker(rank, world, port, q):
         wv, wi = otk.topk(x, 50)
         ok_topk = (torch.equal(indices.cpu(), wi) and torch.equal(values.cpu(), wv) and
                    torch.equal(i2.cpu(), wi) and torch.equal(v2.cpu(), wv))
+        peer = sharded.PeerVocabShardedTopK(x.shape[0], 50, device=dev)
+        for call in range(5):
+            xs = x if call % 2 == 0 else x.to(torch.bfloat16)
+            pv, pi = peer(xs[:, lo:hi].contiguous().to(dev), lo)
+            bv, bi = otk.topk(xs, 50)
+            ok_topk = ok_topk and torch.equal(pi.cpu(), bi) and torch.equal(pv.cpu(), bv)
+        from ckb200 import _native
+        ok_topk = ok_topk and _native.load("topk").ckb_topk_status(1) == 0
+        peer.close()
         inp = workloads.rmsnorm_16384x4096(scale=64)
         r0, r1 = sharded.row_range(inp["x"].shape[0], rank, world)
         mine = rmsnorm.rmsnorm(inp["x"][r0:r1].contiguous().to(dev), inp["weight"].to(dev))
@@ -68,7 +78,7 @@ def _worker(rank, world, port, q):
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_vocab_sharded_topk_and_row_shards_over_nccl():
-    world = 2
+    world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()

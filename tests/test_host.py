@@ -83,3 +83,12 @@ def test_row_pipeline_rejects_empty_shapes_before_touching_the_gpu():
         hostpipe.RowPipeline(lambda a, b: None, 0, 8, torch.float32)
     with pytest.raises(ValueError, match="chunks"):
         hostpipe.RowPipeline(lambda a, b: None, 4, 8, torch.float32, chunks=0)
+
+
+def test_exchange_layout_and_epochs():
+    half, lists_off, flags_off = sharded.exchange_layout(8, 512, 50)
+    assert lists_off == 0 and flags_off == 8 * 512 * 50 * 8
+    assert half % 256 == 0 and half >= flags_off + 8 * 512 * 4
+    assert sharded.next_epoch(0) == 1 and sharded.next_epoch(1) == 2
+    e = 0xFFFFFFFF
+    assert sharded.next_epoch(e) == 2 and (sharded.next_epoch(e) & 1) != (e & 1)  # parity keeps alternating
