@@ -497,8 +497,9 @@ def run_vocab(args, rank, world, local):
     shards = [full[:, lo:hi].contiguous().to(dev) for _ in range(2)]  # two copies: rotate past L2
     peer = args.vocab_exchange == "peer"
     op = (sharded.PeerVocabShardedTopK if peer else sharded.VocabShardedTopK)(full.shape[0], 50, device=dev)
+    run_step = lambda i: op(shards[i % 2], lo)  # noqa: E731 (eager: one kernel per step on the peer path)
     for i in range(args.warmup):
-        op(shards[i % 2], lo)
+        run_step(i)
     torch.cuda.synchronize()
     barrier(world)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -506,7 +507,7 @@ def run_vocab(args, rank, world, local):
     sampler.__enter__()
     start.record()
     for i in range(args.steps):
-        values, indices = op(shards[i % 2], lo)
+        values, indices = run_step(i)
     end.record()
     torch.cuda.synchronize()
     sampler.__exit__(None, None, None)
@@ -524,7 +525,7 @@ def run_vocab(args, rank, world, local):
                 "config": {"workload": args.workload, "cols_per_gpu": hi - lo, "parallelism": f"vocab-sharded x{world}",
                            "collective": ("fused: the shard kernel stores its [512, 50] composite lists into every "
                                           "rank's memory over NVLink (CUDA IPC) and raises per-row flags; the merge "
-                                          "kernel waits on them" if peer else
+                                          "kernel waits on them and merges, one kernel per step" if peer else
                                           "NCCL all_gather_into_tensor of [512, 50] int64 composites")},
                 "rows_per_s": round(512 * args.steps / (ms * 1e-3), 1),
                 "roofline": {"bound": "hbm", "achieved": round(nbytes / world / (ms / args.steps * 1e-3) / 1e9, 1),

@@ -35,8 +35,8 @@ SIGNATURES = {
         "ckb_topk_shard_launch": (_INT, [_VP] * 4 + [_LL, _LL, _LL, _INT, _INT, _LL, _VP]),
         "ckb_topk_merge_launch": (_INT, [_VP, _INT, _VP, _VP, _LL, _INT, _INT, _VP]),
         "ckb_topk_launch_noalloc": (_INT, [_VP, _VP, _VP, _LL, _LL, _INT, _INT, _VP]),
-        "ckb_topk_shard_push_launch": (_INT, [_VP, _VP, _VP, _LL, _LL, _LL, _INT, _INT, _LL, _PVP, _PVP, _INT, _INT,
-                                              _UINT, _VP]),
+        "ckb_topk_shard_push_launch": (_INT, [_VP] * 5 + [_LL, _LL, _LL, _INT, _INT, _LL, _PVP, _PVP, _INT, _INT,
+                                                           _UINT, _VP]),
         "ckb_topk_merge_wait_launch": (_INT, [_VP, _VP, _INT, _UINT, _VP, _VP, _LL, _INT, _INT, _VP]),
         "ckb_p2p_alloc": (_INT, [_PVP, ctypes.c_ulonglong]),
         "ckb_p2p_free": (_INT, [_VP]),

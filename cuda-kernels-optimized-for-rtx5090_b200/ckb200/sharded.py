@@ -93,6 +93,15 @@ def next_epoch(epoch):
     return e if e <= 0xFFFFFFFF else 2
 
 
+def graph_epochs(epoch):
+    """For a graphed step after epoch `epoch`: the two eager warm-up epochs and the four epochs the graphs carry
+    (replayed in rotation, every call alternates parity and calls two apart differ)."""
+    seq = [epoch]
+    for _ in range(6):
+        seq.append(next_epoch(seq[-1]))
+    return seq[1:3], seq[3:]
+
+
 class PeerVocabShardedTopK:
     """The vocab-sharded top-k with its all-gather done by the kernels over peer memory.
 
@@ -138,25 +147,69 @@ class PeerVocabShardedTopK:
                 self.bases.append(ptr.value)
                 self._imported.append(ptr.value)
         self.epoch = 0
+        self._graphs = []
 
     def __call__(self, x_shard, col_offset):
         """(values, int64 indices) [rows, k] of the full rows; x_shard [rows, local_cols] holds global columns
-        [col_offset, col_offset + local_cols). Launches two kernels on the current stream, no collective call."""
+        [col_offset, col_offset + local_cols). One kernel on the current stream (two when its CTAs do not all fit
+        the GPU at once), no collective call."""
+        self.epoch = next_epoch(self.epoch)
+        return self._step(x_shard, col_offset, self.epoch)
+
+    def _step(self, x_shard, col_offset, epoch, values=None, indices=None):
         if x_shard.shape[0] != self.rows:
             raise ValueError(f"PeerVocabShardedTopK: {x_shard.shape[0]} rows, built for {self.rows}")
-        self.epoch = next_epoch(self.epoch)
-        par = (self.epoch & 1) * self.half
+        par = (epoch & 1) * self.half
         lists = [b + par + self.lists_off for b in self.bases]
         flags = [b + par + self.flags_off for b in self.bases]
-        _topk.shard_push(x_shard, col_offset, self.k, lists, flags, self.rank, self.epoch)
-        return _topk.merge_wait(lists[self.rank], flags[self.rank], self.world, self.epoch, self.rows, self.k,
-                                x_shard.dtype, x_shard.device)
+        if values is None:
+            values = torch.empty((self.rows, self.k), dtype=x_shard.dtype, device=x_shard.device)
+            indices = torch.empty((self.rows, self.k), dtype=torch.int64, device=x_shard.device)
+        _topk.shard_push(x_shard, col_offset, self.k, lists, flags, self.rank, epoch, values, indices)
+        return values, indices
+
+    def graphed(self, x_shards, col_offset):
+        """A replayable step on fixed buffers: four CUDA graphs carrying the next four epochs of this object's
+        sequence, replayed in rotation by the returned callable, which gives the (values, indices) tensors it
+        rewrites. x_shards is one shard tensor or a list of 1, 2 or 4 of them (graph j reads x_shards[j % n], so two
+        copies alternate). The rotation keeps what the equal-flag waits need: consecutive calls alternate parity and
+        calls two apart carry different epochs. Every rank must capture and replay in step; no eager call may
+        follow."""
+        shards = list(x_shards) if isinstance(x_shards, (list, tuple)) else [x_shards]
+        if len(shards) not in (1, 2, 4):
+            raise ValueError(f"PeerVocabShardedTopK.graphed: 1, 2 or 4 inputs, got {len(shards)}")
+        x0 = shards[0]
+        values = torch.empty((self.rows, self.k), dtype=x0.dtype, device=x0.device)
+        indices = torch.empty((self.rows, self.k), dtype=torch.int64, device=x0.device)
+        warm, captured = graph_epochs(self.epoch)
+        for j, e in enumerate(warm):  # two eager steps: plan, workspace and counters exist before capture
+            self._step(shards[j % len(shards)], col_offset, e, values, indices)
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        graphs = []
+        for j, e in enumerate(captured):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._step(shards[j % len(shards)], col_offset, e, values, indices)
+            graphs.append(g)
+        self.epoch = captured[-1]
+        self._graphs = graphs
+        state = {"i": 0}
+
+        def replay():
+            graphs[state["i"] % 4].replay()
+            state["i"] += 1
+            return values, indices
+
+        return replay
 
     def close(self):
         """Unmaps the peers' buffers and frees this rank's once every rank is done with them."""
         if self._own is None:
             return
         torch.cuda.synchronize(self.device)
+        self._graphs = []
         if self.world > 1:
             dist.barrier(group=self.group)
         with torch.cuda.device(self.device):

@@ -133,15 +133,18 @@ def merge_lists(lists, dtype, k=K):
     return values, indices
 
 
-def shard_push(x, col_offset, k, lists_ptrs, flags_ptrs, rank, epoch):
+def shard_push(x, col_offset, k, lists_ptrs, flags_ptrs, rank, epoch, values=None, indices=None):
     """Local half of the vocab-sharded top-k over peer memory: the shard's row lists go to slot `rank` of every
     rank's exchange buffer (lists_ptrs / flags_ptrs: one device address per rank, this call's parity) and each row's
-    flag is set to `epoch` there (ckb_topk_shard_push_launch)."""
+    flag is set to `epoch` there (ckb_topk_shard_push_launch). With values / indices ([rows, k] in x's dtype and
+    int64) the final top k of the full rows is written too (in the same kernel when its CTAs fit the GPU at once)."""
     import ctypes
 
     dtype = _check_x(x, k)
     x = x.contiguous()
     rows, cols = x.shape
+    if (values is None) != (indices is None):
+        raise ValueError("topk shard push: give both values and indices, or neither")
     chunk, work = _plan(x, rows, cols, dtype, k)
     counters = _row_counters(x.device, rows)
     world = len(lists_ptrs)
@@ -149,9 +152,10 @@ def shard_push(x, col_offset, k, lists_ptrs, flags_ptrs, rank, epoch):
     flags_arr = (ctypes.c_void_p * world)(*flags_ptrs)
     lib = _native.load("topk")
     with torch.cuda.device(x.device):
-        err = lib.ckb_topk_shard_push_launch(x.data_ptr(), work.data_ptr(), counters.data_ptr(), rows, cols,
-                                             int(col_offset), k, dtype, chunk, lists_arr, flags_arr, world, rank,
-                                             epoch, _native.stream_of(x))
+        err = lib.ckb_topk_shard_push_launch(x.data_ptr(), None if values is None else values.data_ptr(),
+                                             None if indices is None else indices.data_ptr(), work.data_ptr(),
+                                             counters.data_ptr(), rows, cols, int(col_offset), k, dtype, chunk,
+                                             lists_arr, flags_arr, world, rank, epoch, _native.stream_of(x))
     _native.check(err)
 
 

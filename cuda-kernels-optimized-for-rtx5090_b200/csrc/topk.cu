@@ -559,9 +559,11 @@ __device__ __forceinline__ u64 raise_bound(u64 lo, u64 kth) {
 
 constexpr int kMaxPeers = 8;
 
-// Mode 2 (vocab-sharded top-k over peer memory): each rank's exchange buffer holds, for the current call's parity,
-// lists [world][rows][k] and flags [world][rows]; this rank writes its row lists into slot `rank` of every rank's
-// buffer and then sets flag [rank][row] = epoch there.
+// Modes 2 and 3 (vocab-sharded top-k over peer memory): each rank's exchange buffer holds, for the current call's
+// parity, lists [world][rows][k] and flags [world][rows]; this rank writes its row lists into slot `rank` of every
+// rank's buffer and then sets flag [rank][row] = epoch there. Mode 3 then also waits, per row, for every rank's list
+// of the row in its own buffer and writes the merged top k (values / indices as mode 0). Flags are compared for
+// equality: consecutive calls alternate parity, and any two calls on one parity carry different epochs.
 struct PushArgs {
   u64* lists[kMaxPeers];        // every rank's lists base for this parity (this rank's own included)
   unsigned* flags[kMaxPeers];   // every rank's flags base for this parity
@@ -605,10 +607,52 @@ __device__ __forceinline__ void emit(const SegArgs& a, long long row, int j, u64
   }
 }
 
-// Mode 2, after every emit of the row: the writers' stores are made visible system-wide before the row's flag moves
-// on each rank (the block barrier orders every writer's fence before the flag stores).
+// Mode 3, once the row is published: thread p < world waits (bounded) until rank p's list of the row is in this
+// rank's buffer, then the block ranks the world lists in shared memory `sl` (world * k entries) and writes the row's
+// final top k. The lists are read through L2: peers wrote them during this kernel's life.
+template <typename T>
+__device__ void merge_published(const SegArgs& a, long long row, int tid, int nthreads, u64* sl, int* s_timeout) {
+  const int world = a.push.world, k = a.k;
+  const long long rows = a.push.rows;
+  if (tid < world) {
+    const unsigned* f = a.push.flags[a.push.rank] + (long long)tid * rows + row;
+    if (ld_acquire_sys(f) != a.push.epoch) {
+      const unsigned long long start = global_ns();
+      while (ld_acquire_sys(f) != a.push.epoch) {
+        if (global_ns() - start > kWaitLimitNs) {
+          *s_timeout = 1;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  __syncthreads();
+  if (*s_timeout && tid == 0) atomicOr(&g_topk_status, CKB_STATUS_TIMEOUT);
+  const u64* own = a.push.lists[a.push.rank];
+  for (int i = tid; i < world * k; i += nthreads) {
+    const int l = i / k, j = i - l * k;
+    sl[i] = __ldcg(own + ((long long)l * rows + row) * k + j);
+  }
+  __syncthreads();
+  for (int i = tid; i < world * k; i += nthreads) {
+    const u64 c = sl[i];
+    if (c == 0ull) continue;
+    const int mine = i / k;
+    int rank = i - mine * k;
+    for (int l = 0; l < world && rank < k; ++l)
+      if (l != mine) rank += count_greater(sl + l * k, k, c);
+    if (rank < k) {
+      reinterpret_cast<T*>(a.values)[row * k + rank] = decode_value<T>(c);
+      a.indices[row * k + rank] = decode_index(c);
+    }
+  }
+}
+
+// Modes 2 and 3, after every emit of the row: the writers' stores (threads below k) are made visible system-wide
+// before the row's flag moves on each rank (the block barrier orders every writer's fence before the flag stores).
 __device__ __forceinline__ void publish_row(const SegArgs& a, long long row, int tid) {
-  __threadfence_system();
+  if (tid < a.k) __threadfence_system();
   __syncthreads();
   if (tid < a.push.world) st_release_sys(a.push.flags[tid] + (long long)a.push.rank * a.push.rows + row, a.push.epoch);
 }
@@ -631,7 +675,9 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   __shared__ int s_flag[3];  // tile j >= 1: bit 0 some warp's slots are half full, bit 1 some warp's overflowed
   __shared__ int s_pack;
   __shared__ int s_last;
+  __shared__ int s_timeout;  // mode 3: a wait for a peer's list ran out
 
+  if (threadIdx.x == 0) s_timeout = 0;
   const T* tag = nullptr;
   uint4* ring = reinterpret_cast<uint4*>(smem_raw);
   u64* cand = reinterpret_cast<u64*>(smem_raw + kRingBytes);  // running top at [0, ntop), survivors behind it
@@ -882,7 +928,8 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   // Output, or the multi-segment merge by the row's last CTA.
   if (nseg == 1) {
     for (int i = tid; i < k; i += kThreads) emit<T>(a, row, i, cand[i]);
-    if (a.mode == 2) publish_row(a, row, tid);
+    if (a.mode >= 2) publish_row(a, row, tid);
+    if (a.mode == 3) merge_published<T>(a, row, tid, kThreads, reinterpret_cast<u64*>(smem_raw), &s_timeout);
     return;
   }
   u64* wr = a.work + ((long long)row * nseg + seg) * k;
@@ -919,7 +966,8 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   }
   for (int i = tid; i < k; i += kThreads) emit<T>(a, row, i, la[i]);
   if (tid == 0) a.counters[row] = 0u;
-  if (a.mode == 2) publish_row(a, row, tid);
+  if (a.mode >= 2) publish_row(a, row, tid);  // its barrier also ends every read of la / lb in the ring
+  if (a.mode == 3) merge_published<T>(a, row, tid, kThreads, reinterpret_cast<u64*>(smem_raw), &s_timeout);
 }
 
 // Merge of nlists sorted composite lists per row, lists laid out [nlists][rows][k] (an all-gather's output); one
@@ -964,9 +1012,9 @@ __global__ void __launch_bounds__(256) topk_merge_wait(const u64* lists, const u
   __syncthreads();
   if (threadIdx.x < world) {
     const unsigned* f = flags + (long long)threadIdx.x * rows + row;
-    if ((int)(ld_acquire_sys(f) - epoch) < 0) {
+    if (ld_acquire_sys(f) != epoch) {
       const unsigned long long start = global_ns();
-      while ((int)(ld_acquire_sys(f) - epoch) < 0) {
+      while (ld_acquire_sys(f) != epoch) {
         if (global_ns() - start > kWaitLimitNs) {
           s_timeout = 1;
           break;
@@ -1055,6 +1103,26 @@ int start_seg(const SegArgs& a, long long rows, long long nseg, cudaStream_t s) 
 
 long long segments(long long cols, long long chunk) { return (cols + chunk - 1) / chunk; }
 
+// CTAs of the shape start_seg picks that the GPU holds at once (0 on error).
+template <typename T, int NT>
+long long resident_ctas() {
+  if (prepare_stream_kernel<T, NT>() != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, topk_stream<T, NT>, NT, Cfg<NT, sizeof(T)>::kSmemBytes) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return (long long)per_sm * device_sm_count();
+}
+template <typename T>
+long long resident_for(long long rows, int k) {
+  return narrow_for(rows, k) ? resident_ctas<T, 256>() : resident_ctas<T, 512>();
+}
+
 // The reference's argument checks (topk/kernel.cu:551-554) plus this library's limits: an element-aligned x and
 // at most the shape's merge capacity (segments x k composites) for a split row.
 bool bad_args(const void* x, long long rows, long long cols, int k, long long chunk, int elem) {
@@ -1141,22 +1209,26 @@ CKB_EXPORT int ckb_topk_merge_launch(const unsigned long long* lists, int nlists
   return (int)cudaGetLastError();
 }
 
-// Vocab-sharded variant over peer memory, local half (no counterpart in the reference): as ckb_topk_shard_launch,
-// but each row's sorted list goes to slot `rank` of every rank's exchange buffer (lists[p] + (rank * rows + row) * k
-// for p < world, NVLink stores) and flags[p][rank * rows + row] is then set to `epoch` (release, system scope).
-// lists / flags are host arrays of `world` device pointers (this call's parity of each rank's buffer, this rank's
-// own included). 1 <= world <= 8, 0 <= rank < world, epoch != 0.
-CKB_EXPORT int ckb_topk_shard_push_launch(const void* x, void* work, void* counters, long long rows, long long cols,
-                                          long long col_offset, int k, int dtype, long long chunk,
-                                          unsigned long long* const* lists, unsigned* const* flags, int world,
-                                          int rank, unsigned epoch, cudaStream_t stream) {
+// Vocab-sharded variant over peer memory (no counterpart in the reference): as ckb_topk_shard_launch, but each row's
+// sorted list goes to slot `rank` of every rank's exchange buffer (lists[p] + (rank * rows + row) * k for p < world,
+// NVLink stores) and flags[p][rank * rows + row] is then set to `epoch` (release, system scope). lists / flags are
+// host arrays of `world` device pointers (this call's parity of each rank's buffer, this rank's own included).
+// With values / indices null that is all (ckb_topk_merge_wait_launch merges later). With them, the final top k of
+// the full rows is written too: by the same kernel when all of its CTAs fit on the GPU at once (each row's CTA waits
+// for the other ranks' lists of its row, then merges), otherwise by a merge-wait launch behind it on `stream`.
+// 1 <= world <= 8, 0 <= rank < world, epoch != 0.
+CKB_EXPORT int ckb_topk_shard_push_launch(const void* x, void* values, void* indices, void* work, void* counters,
+                                          long long rows, long long cols, long long col_offset, int k, int dtype,
+                                          long long chunk, unsigned long long* const* lists, unsigned* const* flags,
+                                          int world, int rank, unsigned epoch, cudaStream_t stream) {
   if (rows <= 0 || k <= 0) return 0;
   if (dtype != kF32 && dtype != kBF16) return -1;
   if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world || epoch == 0u || !lists || !flags) return -1;
+  if ((values == nullptr) != (indices == nullptr)) return -1;
   const int elem = dtype == kBF16 ? 2 : 4;
   if (col_offset < 0 || col_offset + cols > INT_MAX / 2 || bad_args(x, rows, cols, k, chunk, elem)) return -1;
   if (chunk > cols) chunk = cols;
-  SegArgs a{x, nullptr, nullptr, nullptr, (u64*)work, (unsigned*)counters, col_offset, (int)cols, k, 2, {}};
+  SegArgs a{x, values, (long long*)indices, nullptr, (u64*)work, (unsigned*)counters, col_offset, (int)cols, k, 2, {}};
   for (int p = 0; p < world; ++p) {
     if (!lists[p] || !flags[p]) return -1;
     a.push.lists[p] = (u64*)lists[p];
@@ -1166,8 +1238,14 @@ CKB_EXPORT int ckb_topk_shard_push_launch(const void* x, void* work, void* count
   a.push.rank = rank;
   a.push.epoch = epoch;
   a.push.rows = rows;
-  if (dtype == kF32) return start_seg<float>(a, rows, segments(cols, chunk), stream);
-  return start_seg<__nv_bfloat16>(a, rows, segments(cols, chunk), stream);
+  const long long nseg = segments(cols, chunk);
+  if (values) {
+    const long long cap = dtype == kF32 ? resident_for<float>(rows, k) : resident_for<__nv_bfloat16>(rows, k);
+    if (rows * nseg <= cap) a.mode = 3;
+  }
+  const int err = dtype == kF32 ? start_seg<float>(a, rows, nseg, stream) : start_seg<__nv_bfloat16>(a, rows, nseg, stream);
+  if (err || !values || a.mode == 3) return err;
+  return ckb_topk_merge_wait_launch(lists[rank], flags[rank], world, epoch, values, indices, rows, k, dtype, stream);
 }
 
 // Vocab-sharded variant over peer memory, merge half (no counterpart in the reference): lists [world][rows][k] and
@@ -1229,9 +1307,8 @@ CKB_EXPORT int ckb_p2p_import(const void* handle, void** ptr) {
 }
 CKB_EXPORT int ckb_p2p_close(void* ptr) { return (int)cudaIpcCloseMemHandle(ptr); }
 
-// Status word of this library's kernels since the last reset (0 = fine). The streaming kernel waits only on its own
-// asynchronous copies, which always complete, so nothing sets it today; the entry point stays for callers that poll
-// it. Synchronises with the device; reset != 0 clears the word.
+// Status word of this library's kernels since the last reset: 0 fine, 1 when a wait on a peer's per-row flag (the
+// vocab-sharded variant over peer memory) ran out. Synchronises with the device; reset != 0 clears the word.
 CKB_EXPORT int ckb_topk_status(int reset) {
   unsigned v = 0;
   cudaError_t e = cudaMemcpyFromSymbol(&v, g_topk_status, sizeof(v));

@@ -39,13 +39,18 @@ int ckb_topk_merge_launch(const unsigned long long* lists, int nlists, void* val
  * Local half: as ckb_topk_shard_launch, but every row's sorted list is stored into slot `rank` of every rank's lists
  * (NVLink stores) and then flags[p][rank * rows + row] = epoch on every rank p (release, system scope). lists / flags:
  * host arrays of `world` device pointers to this parity's half of each rank's buffer (this rank's own included).
- * 1 <= world <= 8, 0 <= rank < world, epoch != 0 (callers count calls from 1; parity = epoch & 1). */
-int ckb_topk_shard_push_launch(const void* x, void* work, void* counters, long long rows, long long cols,
-                               long long col_offset, int k, int dtype, long long chunk,
+ * values / indices (both null, or both set): when set, the final top k of the full rows [rows, k] (x's dtype, int64)
+ * is written too, by the same kernel when all of its CTAs fit on the GPU at once (each row waits for the other
+ * ranks' lists of the row in this rank's buffer, then merges; waits bounded as below), otherwise by a
+ * ckb_topk_merge_wait_launch queued behind it. 1 <= world <= 8, 0 <= rank < world, epoch != 0; flags are compared
+ * for equality, so successive calls must alternate parity (half = epoch & 1) and two calls on one half must carry
+ * different epochs (counting calls from 1 does both; so does cycling 1, 2, 3, 4). */
+int ckb_topk_shard_push_launch(const void* x, void* values, void* indices, void* work, void* counters, long long rows,
+                               long long cols, long long col_offset, int k, int dtype, long long chunk,
                                unsigned long long* const* lists, unsigned* const* flags, int world, int rank,
                                unsigned epoch, cudaStream_t stream);
 
-/* Merge half: lists / flags = this rank's own buffer half for this parity. Row r waits until flags[p][r] reaches
+/* Merge half: lists / flags = this rank's own buffer half for this parity. Row r waits until flags[p][r] equals
  * `epoch` for every rank p (at most 2 s; a wait that runs out sets ckb_topk_status() and the row is merged from
  * whatever is there), then writes values [rows, k] (dtype 0 fp32 / 1 bf16) and int64 indices [rows, k] as
  * ckb_topk_merge_launch. */
@@ -73,9 +78,9 @@ int ckb_p2p_close(void* ptr);
 int ckb_topk_launch_noalloc(const void* x, void* values, void* indices, long long rows, long long cols, int k,
                             int dtype, cudaStream_t stream);
 
-/* Status word of this library's kernels since the last reset (0 fine; the streaming kernel waits only on its own
- * asynchronous copies, which always complete, so nothing sets it today). Synchronous; reset != 0 clears it; negative:
- * -cudaError_t. No counterpart in the reference. */
+/* Status word of this library's kernels since the last reset: 0 fine, 1 a peer-memory wait (the vocab-sharded
+ * variant's per-row flags) ran out. Synchronous; reset != 0 clears it; negative: -cudaError_t. No counterpart in the
+ * reference. */
 int ckb_topk_status(int reset);
 
 #ifdef __cplusplus

@@ -56,6 +56,11 @@ def _worker(rank, world, port, q):
             pv, pi = peer(xs[:, lo:hi].contiguous().to(dev), lo)
             bv, bi = otk.topk(xs, 50)
             ok_topk = ok_topk and torch.equal(pi.cpu(), bi) and torch.equal(pv.cpu(), bv)
+        step = peer.graphed(x[:, lo:hi].contiguous().to(dev), lo)
+        for call in range(6):
+            gv, gi = step()
+            torch.cuda.synchronize()
+            ok_topk = ok_topk and torch.equal(gi.cpu(), wi) and torch.equal(gv.cpu(), wv)
         from ckb200 import _native
         ok_topk = ok_topk and _native.load("topk").ckb_topk_status(1) == 0
         peer.close()

@@ -1,5 +1,6 @@
 """The peer-memory vocab-sharded top-k kernels on one GPU: W ranks emulated in one process, every rank's exchange
-buffer on this GPU, every push queued before any merge (so no kernel waits on one that has not run). Each rank's
+buffer on this GPU, every push queued before any merge (so no kernel waits on one that has not run; the fused
+push-and-merge kernel, which waits inside, is only run here with one rank). Each rank's
 merge must give the single-GPU top-k of the full rows bit for bit, over several epochs (both parity halves).
 The bounded wait: a merge whose flags nothing sets gives up after its limit and reports through the status word."""
 
@@ -69,6 +70,24 @@ def test_single_rank_class_repeated_calls():
             v, i = op(x.cuda(), 0)
             wv, wi = otk.topk(x, 50)
             assert torch.equal(i.cpu(), wi) and torch.equal(v.cpu(), wv)
+    finally:
+        op.close()
+
+
+def test_single_rank_fused_kernel_and_graph_replays():
+    """One rank: the shard kernel merges in place (it waits only on its own flags); four captured graphs replayed in
+    rotation keep giving the same answer."""
+    x = torch.randn(512, 30011, generator=torch.Generator().manual_seed(6))
+    xd = x.cuda()
+    op = sharded.PeerVocabShardedTopK(512, 50)
+    try:
+        step = op.graphed(xd, 0)
+        wv, wi = otk.topk(x, 50)
+        for _ in range(9):
+            v, i = step()
+            torch.cuda.synchronize()
+            assert torch.equal(i.cpu(), wi) and torch.equal(v.cpu(), wv)
+        assert _native.load("topk").ckb_topk_status(1) == 0
     finally:
         op.close()
 

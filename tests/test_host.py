@@ -92,3 +92,12 @@ def test_exchange_layout_and_epochs():
     assert sharded.next_epoch(0) == 1 and sharded.next_epoch(1) == 2
     e = 0xFFFFFFFF
     assert sharded.next_epoch(e) == 2 and (sharded.next_epoch(e) & 1) != (e & 1)  # parity keeps alternating
+
+
+@pytest.mark.parametrize("start", [0, 5, 0xFFFFFFFA, 0xFFFFFFFD])
+def test_graph_epoch_rotation_alternates_parity_and_never_repeats_two_apart(start):
+    warm, captured = sharded.graph_epochs(start)
+    seq = [start] + warm + captured * 4
+    assert 0 not in seq[1:]
+    assert all((a & 1) != (b & 1) for a, b in zip(seq, seq[1:]))
+    assert all(a != c for a, c in zip(seq[1:], seq[3:]))
