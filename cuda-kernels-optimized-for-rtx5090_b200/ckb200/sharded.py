@@ -108,11 +108,12 @@ class PeerVocabShardedTopK:
     Every rank allocates one exchange buffer (two parity halves, exchange_layout) through the top-k library, and the
     ranks swap CUDA IPC handles once (a host all-gather of 64-byte handles), so each holds every rank's buffer
     address. A call with epoch e (counted from 1) uses half e & 1: ckb_topk_shard_push_launch stores this rank's
-    row lists into slot `rank` of every rank's half and sets the row flags to e there, then
-    ckb_topk_merge_wait_launch waits on this rank's own flags and merges. Two halves suffice: a rank starts call
-    e + 2 only after its merge of call e + 1 saw every rank's lists of e + 1, which those ranks pushed after
-    finishing their merges of call e. Call close() on every rank (it synchronises them) before the process group
-    goes."""
+    row lists into slot `rank` of every rank's half and sets the row flags to e there; in the same kernel each row
+    then waits on this rank's own flags and merges (a merge-wait kernel follows instead when the kernel's CTAs do
+    not all fit the GPU at once). Two halves suffice: a rank starts call e + 2 only after its merge of call e + 1
+    saw every rank's lists of e + 1, which those ranks pushed after finishing their merges of call e. The launch
+    arguments are checked and packed once per shard shape, so a call costs one library call and the two output
+    allocations. Call close() on every rank (it synchronises them) before the process group goes."""
 
     def __init__(self, rows, k=_topk.K, device=None, group=None):
         self.group = group
@@ -148,6 +149,7 @@ class PeerVocabShardedTopK:
                 self._imported.append(ptr.value)
         self.epoch = 0
         self._graphs = []
+        self._args = {}
 
     def __call__(self, x_shard, col_offset):
         """(values, int64 indices) [rows, k] of the full rows; x_shard [rows, local_cols] holds global columns
@@ -156,16 +158,43 @@ class PeerVocabShardedTopK:
         self.epoch = next_epoch(self.epoch)
         return self._step(x_shard, col_offset, self.epoch)
 
-    def _step(self, x_shard, col_offset, epoch, values=None, indices=None):
+    def _launch_args(self, x_shard):
+        """Everything a call passes to ckb_topk_shard_push_launch but x, the outputs and the epoch, for this shard's
+        shape (checked, planned and packed once): (dtype code, cols, chunk, work, counters, lists and flags pointer
+        arrays per parity)."""
+        key = (tuple(x_shard.shape), x_shard.dtype, x_shard.device)
+        hit = self._args.get(key)
+        if hit is not None:
+            return hit
         if x_shard.shape[0] != self.rows:
             raise ValueError(f"PeerVocabShardedTopK: {x_shard.shape[0]} rows, built for {self.rows}")
-        par = (epoch & 1) * self.half
-        lists = [b + par + self.lists_off for b in self.bases]
-        flags = [b + par + self.flags_off for b in self.bases]
+        dtype = _topk._check_x(x_shard, self.k)
+        rows, cols = x_shard.shape
+        chunk, work = _topk._plan(x_shard, rows, cols, dtype, self.k)
+        counters = _topk._row_counters(x_shard.device, rows)
+        arrays = []
+        for par in (0, 1):
+            off = par * self.half
+            lists = (ctypes.c_void_p * self.world)(*[b + off + self.lists_off for b in self.bases])
+            flags = (ctypes.c_void_p * self.world)(*[b + off + self.flags_off for b in self.bases])
+            arrays.append((lists, flags))
+        hit = (dtype, cols, chunk, work, counters, arrays)
+        self._args[key] = hit
+        return hit
+
+    def _step(self, x_shard, col_offset, epoch, values=None, indices=None):
+        if not x_shard.is_contiguous():
+            x_shard = x_shard.contiguous()
+        dtype, cols, chunk, work, counters, arrays = self._launch_args(x_shard)
         if values is None:
             values = torch.empty((self.rows, self.k), dtype=x_shard.dtype, device=x_shard.device)
             indices = torch.empty((self.rows, self.k), dtype=torch.int64, device=x_shard.device)
-        _topk.shard_push(x_shard, col_offset, self.k, lists, flags, self.rank, epoch, values, indices)
+        lists, flags = arrays[epoch & 1]
+        err = self._lib.ckb_topk_shard_push_launch(x_shard.data_ptr(), values.data_ptr(), indices.data_ptr(),
+                                                   work.data_ptr(), counters.data_ptr(), self.rows, cols,
+                                                   int(col_offset), self.k, dtype, chunk, lists, flags, self.world,
+                                                   self.rank, epoch, torch.cuda.current_stream(self.device).cuda_stream)
+        _native.check(err)
         return values, indices
 
     def graphed(self, x_shards, col_offset):
