@@ -516,17 +516,44 @@ __device__ __forceinline__ void select_top(const u64* cand, int cnt, int k, u64*
   __syncthreads();
 }
 
+// select_top when cand[0, np) is already sorted descending (the running top of the last compaction) and only
+// cand[np, cnt) is new: an entry of the sorted prefix ranks at its index plus the new entries above it; a new entry
+// at the prefix entries above it (binary search) plus the other new entries above it. Each rank counts cnt - np
+// entries instead of cnt.
+template <int NT>
+__device__ __forceinline__ void select_top_sorted_prefix(const u64* cand, int np, int cnt, int k, u64* top) {
+  int g = 32;
+  while (g > 1 && cnt * g > NT) g >>= 1;
+  const int sub = threadIdx.x & (g - 1);
+  for (int base = 0; base < cnt; base += NT / g) {  // uniform trip count: every lane joins the shuffles
+    const int item = base + (int)threadIdx.x / g;
+    u64 c = 0ull;
+    int rank = 0;
+    if (item < cnt) {
+      c = cand[item];
+#pragma unroll 4
+      for (int j = np + sub; j < cnt; j += g) rank += cand[j] > c;
+      if (sub == 0) rank += item < np ? item : count_greater(cand, np, c);
+    }
+    for (int o = g >> 1; o > 0; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
+    if (item < cnt && sub == 0 && rank < k) top[rank] = c;
+  }
+  for (int e = cnt + threadIdx.x; e < k; e += NT) top[e] = 0ull;
+  __syncthreads();
+}
+
 // Compaction: the top k of the n distinct composites in cand[0, n), sorted, into cand[0, k) (zero padded when
-// n < k); returns min(k, n). Up to cap = max(k + 32, kDirectSelect) candidates (at most kPack) go straight to the
+// n < k); returns min(k, n). cand[0, np) must be sorted descending (np = 0: no such prefix). Up to cap = max(k + 32, kDirectSelect) candidates (at most kPack) go straight to the
 // rank count, whose cost grows with the square of the count; more are first narrowed by a radix select to at most
 // cap, packed into tmp. tmp (kPack entries) is scratch. All threads call it; ends with a barrier.
 template <int NT>
-__device__ int compact(u64* cand, int n, int k, u64* tmp, unsigned* warp_tot, int* s_bin, unsigned* s_above,
-                       int* s_pack) {
+__device__ int compact(u64* cand, int np, int n, int k, u64* tmp, unsigned* warp_tot, int* s_bin,
+                       unsigned* s_above, int* s_pack) {
   constexpr int kPack = Cfg<NT>::kPack;
   const int cap = min(kPack, max(kDirectSelect, k + 32));
   if (n <= cap) {
-    select_top<NT>(cand, n, k, tmp);
+    if (np > 0) select_top_sorted_prefix<NT>(cand, np, n, k, tmp);
+    else select_top<NT>(cand, n, k, tmp);
     for (int i = threadIdx.x; i < k; i += NT) cand[i] = tmp[i];
     __syncthreads();
     return min(k, n);
@@ -771,7 +798,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   // The top k of cand, a guaranteed bound from its k-th entry and, speculating, a speculative one from its m-th
   // (after `seen` elements of the segment).
   auto compact_all = [&](float seen) {  // seen < 0: no speculative bound
-    ntop = compact<NT>(cand, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
+    ntop = compact<NT>(cand, ntop, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
     filled = 0;
     if (ntop == k) {
       lo = raise_bound(lo, cand[k - 1]);
@@ -794,7 +821,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
     __syncthreads();
     if (ntop + filled + s_cnt > kCand) {
       __syncthreads();  // every thread has read s_cnt
-      ntop = compact<NT>(cand, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
+      ntop = compact<NT>(cand, ntop, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
       filled = 0;
       if (ntop == k) lo = raise_bound(lo, cand[k - 1]);
       const u64 edge = radix_edge<NT>([&](auto&& f) { for_each_at_least(t, lo, f); }, (unsigned)k, kCand - ntop,
@@ -919,7 +946,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
       fs = fnext;
     }
     expand_all(wcnt);
-    if (filled > 0) ntop = compact<NT>(cand, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
+    if (filled > 0) ntop = compact<NT>(cand, ntop, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
     cp_async_wait<0>();
     if (spec == 0ull || (ntop == k && cand[k - 1] >= spec)) break;
     __syncthreads();  // every thread has read cand[k - 1] before the second pass clears the buffer
