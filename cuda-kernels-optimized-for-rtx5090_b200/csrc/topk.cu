@@ -1178,7 +1178,8 @@ CKB_EXPORT long long plan(long long rows, long long cols, int dtype, int threads
 
 // Replaces the reference's top-k `launch` (topk/kernel.cu:549-570): same arguments, checks and return codes. work is
 // int64 [rows * segments * k] (unused with one segment), counters int32 [rows] zeroed once and left zeroed by the
-// kernel. Any chunk >= 1 is served while segments * k <= 6144 (larger gives -1); plan() gives the fastest.
+// kernel. Any chunk >= 1 is served while segments * k fits the last CTA's merge (2048 to 6144 composites by launch
+// shape and dtype; beyond it -1); plan() gives the fastest.
 CKB_EXPORT int launch(const void* x, void* values, void* indices, void* work, void* counters, long long rows,
                       long long cols, int k, int dtype, int threads, int depth, long long chunk,
                       cudaStream_t stream) {
