@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(MAXT) sm_block(const T* __restrict__ x, T* __r
 }
 
 // ---------------------------------------------------------------------------------------------- cluster path ----
-constexpr int kClusterThreads = 256;
+constexpr int kClusterThreads = 384;
 constexpr int kMaxStages = 4;
 
 // The start-up handshake: the initialising thread's fence.mbarrier_init (release, cluster scope) already publishes the
