@@ -61,8 +61,9 @@ def _problem(q, k, cos, sin, ids):
     return None
 
 
-def rope(q, k, position_ids, cos=None, sin=None, theta=None, inplace=False):
-    """Rotates q and k; returns (q_out, k_out). Cache mode with cos/sin, sincos mode with theta."""
+def rope(q, k, position_ids, cos=None, sin=None, theta=None, inplace=False, out=None):
+    """Rotates q and k; returns (q_out, k_out). Cache mode with cos/sin, sincos mode with theta. out = (q_out,
+    k_out) gives the output tensors (contiguous, q's and k's shapes and dtype) instead of new ones."""
     if cos is None and sin is None and theta is None:
         raise ValueError("rope candidate: give the cos/sin cache or theta")
     if (cos is None) != (sin is None):
@@ -77,7 +78,14 @@ def rope(q, k, position_ids, cos=None, sin=None, theta=None, inplace=False):
         q_out, k_out = q, k
     else:
         q, k = q.contiguous(), k.contiguous()
-        q_out, k_out = torch.empty_like(q), torch.empty_like(k)
+        if out is None:
+            q_out, k_out = torch.empty_like(q), torch.empty_like(k)
+        else:
+            q_out, k_out = out
+            for o, t in ((q_out, q), (k_out, k)):
+                if o.shape != t.shape or o.dtype != t.dtype or not o.is_contiguous() or o.device != t.device:
+                    raise ValueError("rope candidate: out must be contiguous tensors of q's and k's shapes, dtype "
+                                     "and device")
     ids = position_ids.contiguous()
     batch, seq, q_heads, head_dim = q.shape
     lib = _native.load("rope")

@@ -1,9 +1,10 @@
-"""Multi-GPU plumbing: row sharding (no communication) and the vocab-sharded top-k (one all-gather).
+"""Multi-GPU plumbing: row and token sharding (no communication) and the vocab-sharded top-k (one all-gather).
 
 One process per GPU (torchrun), torch.distributed over NCCL. The reference is single-GPU; these are the two
 partitionings its row-wise ops admit:
   * rows (tokens, batch entries) are independent for softmax, RMSNorm, RoPE and top-k: rank r owns the contiguous
-    rows row_range(rows, r, world) and runs the single-GPU kernel on them, with no data-path collective;
+    rows row_range(rows, r, world) and runs the single-GPU kernel on them, with no data-path collective (RoPE's
+    rows are the batch x seq tokens, token_shard; its cos/sin cache is replicated);
   * a vocab row split over GPUs (columns col_range(cols, r, world) on rank r) needs one exchange for top-k: each
     rank selects its local top k as sorted 64-bit composites carrying global column indices, an all-gather brings
     every rank's [rows, k] list to every rank ([world, rows, k], world * rows * k * 8 bytes), and the merge kernel
@@ -34,6 +35,18 @@ def split_range(n, rank, world):
 
 row_range = split_range
 col_range = split_range
+token_range = split_range
+
+
+def token_shard(t, rank, world):
+    """Rank `rank`'s contiguous share of the tokens of a [batch, seq, ...] tensor (q, k, or position_ids [batch,
+    seq]): the tokens batch * seq flattened and split by token_range, returned as a [1, n, ...] view (RoPE rotates
+    tokens independently, and the cos/sin cache is replicated on every rank, so a shard needs no exchange)."""
+    if t.dim() < 2 or not t.is_contiguous():
+        raise ValueError(f"token_shard: a contiguous [batch, seq, ...] tensor, got {tuple(t.shape)}")
+    flat = t.reshape(t.shape[0] * t.shape[1], *t.shape[2:])
+    lo, hi = token_range(flat.shape[0], rank, world)
+    return flat[lo:hi].unsqueeze(0)
 
 
 def gather_lists(lists, group=None):
@@ -113,7 +126,15 @@ class PeerVocabShardedTopK:
     not all fit the GPU at once). Two halves suffice: a rank starts call e + 2 only after its merge of call e + 1
     saw every rank's lists of e + 1, which those ranks pushed after finishing their merges of call e. The launch
     arguments are checked and packed once per shard shape, so a call costs one library call and the two output
-    allocations. Call close() on every rank (it synchronises them) before the process group goes."""
+    allocations. Call close() on every rank (it synchronises them) before the process group goes.
+
+    Every wait on a peer's flag is bounded (2 s); a wait that runs out merges whatever the buffer holds, which can be
+    an older call's lists, and records the timeout in the library's status word. check() reads that word (it
+    synchronises the device) and raises; call it after a batch of calls, before trusting their outputs. After a
+    timeout the two-halves invariant no longer holds, so the object refuses further calls: close it on every rank
+    and build a new one (its exchange buffers start zeroed). The in-kernel wait is chosen when all of the kernel's
+    CTAs fit the GPU at once, counted as if nothing else ran on the device; other kernels running beside it (another
+    stream, a collective) delay its CTAs and make a timeout likelier, never a hang."""
 
     def __init__(self, rows, k=_topk.K, device=None, group=None):
         self.group = group
@@ -150,11 +171,15 @@ class PeerVocabShardedTopK:
         self.epoch = 0
         self._graphs = []
         self._args = {}
+        self.broken = False
+        lib.ckb_topk_status(1)  # a timeout recorded before this object existed is not its own
 
     def __call__(self, x_shard, col_offset):
         """(values, int64 indices) [rows, k] of the full rows; x_shard [rows, local_cols] holds global columns
         [col_offset, col_offset + local_cols). One kernel on the current stream (two when its CTAs do not all fit
-        the GPU at once), no collective call."""
+        the GPU at once), no collective call. The outputs are trusted only after check() passes."""
+        if self.broken:
+            raise RuntimeError("PeerVocabShardedTopK: a peer wait timed out earlier; close() and rebuild")
         self.epoch = next_epoch(self.epoch)
         return self._step(x_shard, col_offset, self.epoch)
 
@@ -203,7 +228,9 @@ class PeerVocabShardedTopK:
         rewrites. x_shards is one shard tensor or a list of 1, 2 or 4 of them (graph j reads x_shards[j % n], so two
         copies alternate). The rotation keeps what the equal-flag waits need: consecutive calls alternate parity and
         calls two apart carry different epochs. Every rank must capture and replay in step; no eager call may
-        follow."""
+        follow. check() covers the replays as it covers eager calls."""
+        if self.broken:
+            raise RuntimeError("PeerVocabShardedTopK: a peer wait timed out earlier; close() and rebuild")
         shards = list(x_shards) if isinstance(x_shards, (list, tuple)) else [x_shards]
         if len(shards) not in (1, 2, 4):
             raise ValueError(f"PeerVocabShardedTopK.graphed: 1, 2 or 4 inputs, got {len(shards)}")
@@ -232,6 +259,19 @@ class PeerVocabShardedTopK:
             return values, indices
 
         return replay
+
+    def check(self):
+        """Synchronises this device and raises RuntimeError when any peer-flag wait since the last check ran out (the
+        outputs of the calls since then may hold stale lists); the object is then unusable (close and rebuild)."""
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            status = self._lib.ckb_topk_status(1)
+        if status < 0:
+            raise RuntimeError(f"PeerVocabShardedTopK: status read failed: CUDA error {-status}")
+        if status:
+            self.broken = True
+            raise RuntimeError("PeerVocabShardedTopK: a peer-memory wait ran out (2 s); the outputs since the last "
+                               "check may be stale; close() and rebuild on every rank")
 
     def close(self):
         """Unmaps the peers' buffers and frees this rank's once every rank is done with them."""

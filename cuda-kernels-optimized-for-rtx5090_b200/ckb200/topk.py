@@ -72,15 +72,23 @@ def _check_x(x, k):
     return dtype
 
 
-def topk(x, k=K):
-    """The k largest entries of each row of x, descending, ties by lower index: (values, int64 indices)."""
+def topk(x, k=K, out=None):
+    """The k largest entries of each row of x, descending, ties by lower index: (values, int64 indices), written
+    into out = (values, indices) when given (contiguous [rows, k] tensors of x's dtype and int64)."""
     dtype = _check_x(x, k)
     x = x.contiguous()
     rows, cols = x.shape
     chunk, work = _plan(x, rows, cols, dtype, k)
     counters = _row_counters(x.device, rows)
-    values = torch.empty((rows, k), dtype=x.dtype, device=x.device)
-    indices = torch.empty((rows, k), dtype=torch.int64, device=x.device)
+    if out is None:
+        values = torch.empty((rows, k), dtype=x.dtype, device=x.device)
+        indices = torch.empty((rows, k), dtype=torch.int64, device=x.device)
+    else:
+        values, indices = out
+        for t, dt in ((values, x.dtype), (indices, torch.int64)):
+            if tuple(t.shape) != (rows, k) or t.dtype != dt or not t.is_contiguous() or t.device != x.device:
+                raise ValueError(f"topk candidate: out must be contiguous [rows, k] tensors of {x.dtype} and "
+                                 f"int64 on x's device")
     lib = _native.load("topk")
     with torch.cuda.device(x.device):
         err = lib.launch(x.data_ptr(), values.data_ptr(), indices.data_ptr(), work.data_ptr(), counters.data_ptr(),

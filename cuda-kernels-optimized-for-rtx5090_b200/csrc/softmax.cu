@@ -17,11 +17,12 @@
 //     read comes from L2);
 //   * stream path (unaligned pointers, cols not a multiple of the vector): one block per row reading the row three
 //     times (max, sum, normalise; the later reads mostly from L2).
-// Accuracy (fp32 outputs within 1e-6 relative of an fp64 softmax, elementwise): every path takes exp(x - max) with
-// exp_pair below (relative error within 2.1e-7, measured over every argument; results below FLT_MIN flush to zero).
+// Accuracy (fp32 outputs within 1e-6 relative of an fp64 softmax, elementwise; outputs below FLT_MIN within two
+// subnormal steps): every path takes 2^64 * exp(x - max) with exp_pair below (relative error within about 2.1e-7).
 // Each thread sums its exponentials pairwise per 16-byte vector into an fp64 accumulator, cross-thread and cross-CTA
 // reductions run in fp64, and the output is e * (float)(1 / sum) (or e * (float)(exp(m_c - M) / S) per cluster
-// slice). Maxima propagate NaN, so a row holding a NaN (or +inf, or only -inf) comes out all NaN, as in torch.
+// slice, in two factors when that is below FLT_MIN) with one rounding, so outputs below FLT_MIN are kept as
+// subnormals. Maxima propagate NaN, so a row holding a NaN (or +inf, or only -inf) comes out all NaN, as in torch.
 #include "ckb200_softmax.h"
 #include "common.cuh"
 
@@ -45,12 +46,16 @@ __device__ __forceinline__ void store16(T* p, const float (&f)[VecN<T>::N]) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Packed exponentials: exp(x - M) for two values at a time on the fp32x2 pipe (sm_100); every path uses them.
+// Packed exponentials: 2^64 * exp(x - M) for two values at a time on the fp32x2 pipe (sm_100); every path uses them.
 // Method (from the mathematics; no library routine is restated): TwoSum (Knuth) splits x - M into s + lo exactly;
-// th = s * log2(e) rounded to fp32; E = 2^th by the ex2.approx instruction (flushes results below FLT_MIN to zero);
-// the residual r = (s + lo) - th * ln 2, with ln 2 as a float pair so that r is exact to far below an ulp of E and
-// |r| < 1e-5, is folded in as E * (1 + r) (the dropped r^2 / 2 term is below 1e-10). The relative error is that of
-// ex2.approx plus one rounding. Before the split x is raised to `lowc`, a value below M whose exponential is zero, so
+// tb = s * log2(e) + 384 rounded to fp32 puts th = tb - 384 (exact) on the grid of 2^-15 for every s in the range
+// used (s >= -150 after the clamp below), so th + 64 is exact too; E = 2^(th + 64) by the ex2.approx instruction,
+// which is 2^64 * 2^th without overflow (th <= 0) and normal for th >= -190; the residual r = (s + lo) - th * ln 2,
+// with ln 2 as a float pair so that r is exact to far below an ulp of E and |r| < 1.1e-5, is folded in as E * (1 + r)
+// (the dropped r^2 / 2 term is below 1e-10). The relative error is that of ex2.approx plus one rounding.
+// The 2^64 scale rides through every sum (S' = 2^64 S, so 1 / S' stays a normal float for any row length) and leaves
+// with the final multiplication: each output is E * (1 / S') with one rounding, so results below FLT_MIN come out as
+// subnormals instead of zero. Before the split x is raised to `lowc`, a value below M whose exponential is zero, so
 // that x = -inf gives 0 instead of the inf - inf of the split; a NaN or +inf max makes lowc NaN and every result NaN.
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ float max_nan(float a, float b) {
@@ -84,6 +89,9 @@ __device__ __forceinline__ float2 exp_pair(float2 x, const ExpShift& e) {
   const float2 kL2E = make_float2(1.44269502162933349609375f, 1.44269502162933349609375f);  // fp32(log2 e)
   const float2 kNLn2Hi = make_float2(-0.693147182464599609375f, -0.693147182464599609375f);  // -fp32(ln 2)
   const float2 kNLn2Lo = make_float2(1.904654323148236e-09f, 1.904654323148236e-09f);       // -(ln 2 - fp32(ln 2))
+  const float2 kGrid = make_float2(384.0f, 384.0f);     // 1.5 * 2^8: th lands on the 2^-15 grid
+  const float2 kNGrid = make_float2(-384.0f, -384.0f);
+  const float2 kNGridS = make_float2(-320.0f, -320.0f);  // -384 + 64: the 2^64 scale
   x.x = fmaxf(x.x, e.lowc);
   x.y = fmaxf(x.y, e.lowc);
   const float2 s = __fadd2_rn(x, e.nm);
@@ -92,8 +100,10 @@ __device__ __forceinline__ float2 exp_pair(float2 x, const ExpShift& e) {
   const float2 dx = __ffma2_rn(xb, kNeg1, x);    // x - xb
   const float2 dm = __ffma2_rn(mb, kNeg1, e.nm); // -M - mb
   const float2 lo = __fadd2_rn(dx, dm);          // s + lo == x - M exactly
-  const float2 th = __fmul2_rn(s, kL2E);
-  const float2 E = make_float2(ex2_ftz(th.x), ex2_ftz(th.y));
+  const float2 tb = __ffma2_rn(s, kL2E, kGrid);  // s * log2 e + 384, in [167, 384]
+  const float2 th = __fadd2_rn(tb, kNGrid);      // exact
+  const float2 ts = __fadd2_rn(tb, kNGridS);     // th + 64, exact
+  const float2 E = make_float2(ex2_ftz(ts.x), ex2_ftz(ts.y));
   float2 r = __ffma2_rn(th, kNLn2Hi, s);          // s - th * ln2_hi, exact but for one tiny rounding
   r = __fadd2_rn(r, __ffma2_rn(th, kNLn2Lo, lo)); // + lo - th * ln2_lo
   return __ffma2_rn(E, r, E);
@@ -263,6 +273,40 @@ __device__ __forceinline__ void st_async_u64(unsigned raddr, unsigned long long 
 
 constexpr int kMaxCluster = 16;
 
+// Pass 3 of the cluster path: y = E * s1 (* s2) for the slice held in shared memory (fp32: the exponentials in
+// place; bf16: the raw values, whose exponentials are taken again), streamed to HBM.
+template <typename T, bool kTwo>
+__device__ __forceinline__ void cluster_store(const uint4* buf, uint4* dst, int nv, float s1, float s2,
+                                              const ExpShift& es) {
+  constexpr int V = VecN<T>::N;
+  const float2 m1 = make_float2(s1, s1), m2 = make_float2(s2, s2);
+#pragma unroll 4
+  for (int i = threadIdx.x; i < nv; i += kClusterThreads) {
+    const uint4 raw = buf[i];
+    if constexpr (V == 4) {
+      float2 a = __fmul2_rn(make_float2(__uint_as_float(raw.x), __uint_as_float(raw.y)), m1);
+      float2 b = __fmul2_rn(make_float2(__uint_as_float(raw.z), __uint_as_float(raw.w)), m1);
+      if (kTwo) {
+        a = __fmul2_rn(a, m2);
+        b = __fmul2_rn(b, m2);
+      }
+      st_stream(dst + i, make_uint4(__float_as_uint(a.x), __float_as_uint(a.y), __float_as_uint(b.x),
+                                    __float_as_uint(b.y)));
+    } else {
+      float f[V];
+      unpack16(raw, f, (const T*)nullptr);
+#pragma unroll
+      for (int j = 0; j < V / 2; ++j) {
+        float2 e = __fmul2_rn(exp_pair(make_float2(f[2 * j], f[2 * j + 1]), es), m1);
+        if (kTwo) e = __fmul2_rn(e, m2);
+        f[2 * j] = e.x;
+        f[2 * j + 1] = e.y;
+      }
+      store16(reinterpret_cast<T*>(dst + i), f);
+    }
+  }
+}
+
 // Grid (CL, G), cluster (CL, 1, 1): cluster g handles rows g, g + G, g + 2G, ... and CTA `rank` owns elements
 // [rank * slice, min((rank + 1) * slice, cols)) of each (slice and cols multiples of the 16-byte vector). A CTA cycles
 // its rows through `stages` slice buffers in dynamic shared memory (stride `stage_vec` 16-byte vectors): the bulk copy
@@ -284,7 +328,7 @@ __global__ void __launch_bounds__(kClusterThreads, 3) sm_cluster(const T* __rest
   __shared__ double xsum[2][kMaxCluster];
   __shared__ float red[32];
   __shared__ double red_d[32];
-  __shared__ float scale;
+  __shared__ float scale, scale_lo;
 
   cg::cluster_group cluster = cg::this_cluster();
   const unsigned rank = cluster.block_rank();
@@ -394,34 +438,26 @@ __global__ void __launch_bounds__(kClusterThreads, 3) sm_cluster(const T* __rest
       const double w = lane < (int)csize ? exp((double)ml - (double)M) : 0.0;
       const double S = warp_sum(lane < (int)csize ? xsum[p][lane] * w : 0.0);
       const double wc = __shfl_sync(0xffffffffu, w, (int)rank);
-      if (lane == 0) scale = (float)(wc / S);
-    }
-    __syncthreads();
-    const float f_scale = scale;
-    const float2 scale2 = make_float2(f_scale, f_scale);
-
-    // Pass 3: scale from shared memory, stream to HBM.
-    uint4* const dst = reinterpret_cast<uint4*>(y + row * cols + beg);
-#pragma unroll 4
-    for (int i = threadIdx.x; i < nv; i += kClusterThreads) {
-      const uint4 raw = buf[i];
-      if constexpr (V == 4) {
-        const float2 a = __fmul2_rn(make_float2(__uint_as_float(raw.x), __uint_as_float(raw.y)), scale2);
-        const float2 b = __fmul2_rn(make_float2(__uint_as_float(raw.z), __uint_as_float(raw.w)), scale2);
-        st_stream(dst + i, make_uint4(__float_as_uint(a.x), __float_as_uint(a.y), __float_as_uint(b.x),
-                                      __float_as_uint(b.y)));
-      } else {
-        float f[V];
-        unpack16(raw, f, x);
-#pragma unroll
-        for (int j = 0; j < V / 2; ++j) {
-          const float2 e = __fmul2_rn(exp_pair(make_float2(f[2 * j], f[2 * j + 1]), es), scale2);
-          f[2 * j] = e.x;
-          f[2 * j + 1] = e.y;
+      if (lane == 0) {
+        // Outputs are E * f with E up to 2^64 (exp_pair's scale). A factor f below FLT_MIN would drop bits of normal
+        // outputs, so it is applied as (E * (f * 2^100)) * 2^-100, both factors normal; f below 2^-226 only has
+        // outputs that round to 0. A NaN factor passes through.
+        const double f = wc / S;
+        float hi = (float)f, lo_f = 1.0f;
+        if (f < 0x1p-126) {
+          hi = f >= 0x1p-226 ? (float)(f * 0x1p100) : 0.0f;
+          lo_f = f >= 0x1p-226 ? 0x1p-100f : 1.0f;
         }
-        store16(reinterpret_cast<T*>(dst + i), f);
+        scale = hi;
+        scale_lo = lo_f;
       }
     }
+    __syncthreads();
+
+    // Pass 3: scale from shared memory, stream to HBM (the two-factor form only when the factor needs it).
+    uint4* const dst = reinterpret_cast<uint4*>(y + row * cols + beg);
+    if (scale_lo == 1.0f) cluster_store<T, false>(buf, dst, nv, scale, 1.0f, es);
+    else cluster_store<T, true>(buf, dst, nv, scale, scale_lo, es);
     // Refill this buffer `stages` rows ahead once every thread is done with it (the exponentials written into it by
     // the generic proxy are ordered before the bulk copy's writes by the proxy fence). With no row left for the
     // buffer, the CTA just finishes. The barrier also keeps `scale` and `red` from being rewritten while read.

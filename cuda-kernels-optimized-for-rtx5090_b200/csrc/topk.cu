@@ -1390,10 +1390,12 @@ cudaError_t noalloc_scratch(void** out) {
 // [rows, k] in x's dtype and int64 indices [rows, k] of x [rows, cols], dtype 0 (fp32) or 1 (bf16), planned as plan()
 // would with min_chunk 2048, except that a plan whose split rows would need more than the scratch's 491,520
 // composites of workspace runs each row in one piece. Allocates nothing. Returns 0, -1 for arguments launch() would
-// also reject, -2 for more than 65,536 rows (the scratch's counters), or a cudaError_t.
-// The first call on a device looks up the scratch address (make it before any stream capture). Every call shares the
-// one scratch array, so calls that overlap on the GPU (different streams, no ordering between them) race; calls on
-// one stream are ordered. The counters are cleared on the caller's stream at each call.
+// also reject (more than 65,535 rows among them, so the scratch's 65,536 counters always suffice), or a cudaError_t.
+// The first call on a device looks up the scratch address (make it before any stream capture) and caches it for the
+// life of the process: after a cudaDeviceReset the cached address is stale, so a device reset is not supported once
+// this entry point has been called on that device. Every call shares the one scratch array, so calls that overlap on
+// the GPU (different streams, no ordering between them) race; calls on one stream are ordered. The counters are
+// cleared on the caller's stream at each call.
 CKB_EXPORT int ckb_topk_launch_noalloc(const void* x, void* values, void* indices, long long rows, long long cols,
                                        int k, int dtype, cudaStream_t stream) {
   if (rows <= 0 || k <= 0) return 0;
@@ -1404,7 +1406,7 @@ CKB_EXPORT int ckb_topk_launch_noalloc(const void* x, void* values, void* indice
   if (chunk > cols) chunk = cols;
   long long nseg = segments(cols, chunk);
   if (nseg > 1 && rows * nseg * k > kNoAllocWorkWords) nseg = 1;  // whole rows: no workspace at all
-  if (rows > 2 * kNoAllocCounterWords) return -2;
+  static_assert(2 * kNoAllocCounterWords > 65535, "bad_args() bounds rows by the scratch's counters");
   void* base = nullptr;
   cudaError_t e = noalloc_scratch(&base);
   if (e != cudaSuccess) return (int)e;

@@ -71,10 +71,11 @@ int ckb_p2p_close(void* ptr);
  * through its own fixed-budget allocator, or a path that cannot afford cudaMalloc's device synchronisation): no
  * workspace or counters are passed; a 4 MiB scratch array compiled into this library (held on every GPU that loads
  * it, until exit) serves instead. No counterpart in the reference. dtype 0 fp32 / 1 bf16; returns -1 for arguments
- * launch() rejects, -2 for more than 65,536 rows (beyond the scratch's counters; launch() rejects those anyway). A
- * plan whose split rows would need more workspace than the scratch's 491,520 composites runs each row in one piece
- * instead. The first call on a device looks up the scratch address: make it before any stream capture. All calls
- * share the scratch, so calls that overlap on the GPU race; the counters are cleared on `stream` at every call. */
+ * launch() rejects (more than 65,535 rows among them; the scratch holds a counter for each of those). A plan whose
+ * split rows would need more workspace than the scratch's 491,520 composites runs each row in one piece instead.
+ * The first call on a device looks up the scratch address and keeps it for the life of the process: make that call
+ * before any stream capture, and do not reset the device afterwards. All calls share the scratch, so calls that
+ * overlap on the GPU race; the counters are cleared on `stream` at every call. */
 int ckb_topk_launch_noalloc(const void* x, void* values, void* indices, long long rows, long long cols, int k,
                             int dtype, cudaStream_t stream);
 

@@ -1,6 +1,6 @@
 """Makes the golden fixtures that pin the oracle to the reference's own code.
 
-  python tests/golden/make_golden.py --softmax [--ref /root/reference]
+  python tests/golden/make_golden.py --softmax --ref <reference checkout>
       imports the reference's softmax/baseline.py (its torch implementation) on the CPU and records its outputs in
       fp64 and at the input dtype for seeded inputs -> tests/golden/softmax.npz
   python tests/golden/make_golden.py --gpu [--out DIR]
@@ -159,11 +159,14 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--softmax", action="store_true")
     ap.add_argument("--gpu", action="store_true")
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("CKB_REFERENCE_DIR"),
+                    help="the reference checkout (default: $CKB_REFERENCE_DIR)")
     ap.add_argument("--out", default=HERE)
     a = ap.parse_args()
     os.makedirs(a.out, exist_ok=True)
     if a.softmax:
+        if not a.ref:
+            raise SystemExit("make_golden --softmax: give --ref or set CKB_REFERENCE_DIR")
         make_softmax(a.ref, a.out)
     if a.gpu:
         make_rmsnorm(a.out)

@@ -53,14 +53,19 @@ def assert_ulp(got, want, dtype, max_ulp=1, what=""):
     return d
 
 
-def assert_rel(got, want64, rel, what=""):
-    """|got - want| <= rel * |want| elementwise (want in fp64); NaN exactly where want is NaN."""
+SUBNORMAL_FLOOR = 2.0 ** -148  # two steps of fp32's subnormal spacing (2^-149)
+
+
+def assert_rel(got, want64, rel, what="", floor=SUBNORMAL_FLOOR):
+    """|got - want| <= max(rel * |want|, floor) elementwise (want in fp64); NaN exactly where want is NaN. The floor
+    only matters below fp32's FLT_MIN, where the format's own spacing (2^-149) is coarser than any relative bound
+    near 1e-6: there an output must be within two subnormal steps, so a flushed-to-zero result fails."""
     g = got.detach().cpu().double().numpy()
     w = want64.detach().cpu().numpy()
     assert np.array_equal(np.isnan(g), np.isnan(w)), f"{what}: NaN pattern differs"
     ok = ~np.isnan(w)
     err = np.abs(g[ok] - w[ok])
-    bound = rel * np.abs(w[ok])
+    bound = np.maximum(rel * np.abs(w[ok]), floor)
     bad = err > bound
     assert not bad.any(), (f"{what}: {bad.sum()} elements beyond {rel} relative; worst "
                            f"{(err / np.maximum(np.abs(w[ok]), 1e-300)).max():.3e}")

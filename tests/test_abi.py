@@ -71,6 +71,11 @@ def test_rejected_arguments_return_minus_one():
     assert tk.launch(*([None] * 5), 4, 100000, 50, 0, 256, 4, 0, None) == -1  # chunk
     assert tk.launch(*([None] * 5), 4, 100000, 50, 0, 256, 4, 10, None) == -1  # segments * k beyond the merge
     assert tk.ckb_topk_merge_launch(None, 0, None, None, 4, 50, 0, None) == -1  # no lists
+    # the no-allocation entry rejects what launch() rejects, before it looks up its scratch or touches the GPU
+    assert tk.ckb_topk_launch_noalloc(None, None, None, 65536, 1000, 50, 0, None) == -1  # rows > 65535
+    assert tk.ckb_topk_launch_noalloc(None, None, None, 4, 40, 50, 0, None) == -1  # k > cols
+    assert tk.ckb_topk_launch_noalloc(None, None, None, 4, 1000, 50, 2, None) == -1  # dtype
+    assert tk.ckb_topk_launch_noalloc(None, None, None, 0, 1000, 50, 0, None) == 0  # no rows
 
 
 def test_topk_plan_host_logic():

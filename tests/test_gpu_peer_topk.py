@@ -107,3 +107,25 @@ def test_merge_wait_that_nothing_releases_reports_a_timeout():
         assert lib.ckb_topk_status(0) == 0
     finally:
         buf.free()
+
+
+def test_class_check_raises_after_a_timed_out_wait_and_refuses_further_calls():
+    """A timed-out peer wait is never silent: check() raises, and the object refuses calls until rebuilt. The timeout
+    is made as above (a merge whose peer flag nothing sets), after the object exists, on the same device."""
+    x = torch.randn(16, 4096, generator=torch.Generator().manual_seed(10))
+    op = sharded.PeerVocabShardedTopK(16, 8)
+    buf = _Buffers(2, 1, 8)
+    try:
+        op(x.cuda(), 0)
+        op.check()  # fine so far
+        lists, flags = buf.ptrs(1)
+        tk.merge_wait(lists[0], flags[0], 2, 1, 1, 8, torch.float32, torch.device("cuda"))
+        with pytest.raises(RuntimeError, match="ran out"):
+            op.check()
+        with pytest.raises(RuntimeError, match="rebuild"):
+            op(x.cuda(), 0)
+        assert _native.load("topk").ckb_topk_status(0) == 0  # check() cleared the word
+    finally:
+        torch.cuda.synchronize()
+        buf.free()
+        op.close()
