@@ -135,6 +135,9 @@ class RowPipeline(Pipeline):
         self.x, self.y = self.ins[0], self.outs[0]
 
     def __call__(self, hx, hy):
-        """Queues hx -> op -> hy for every chunk; returns hy (valid after synchronize())."""
+        """Queues hx -> op -> hy for every chunk; returns hy (valid after synchronize()). hx and hy may also be
+        given as one-element lists, as Pipeline takes them."""
+        if isinstance(hx, (list, tuple)):
+            return super().__call__(list(hx), list(hy))
         super().__call__([hx], [hy])
         return hy

@@ -1,5 +1,5 @@
-"""The multi-GPU host path with world_size 2 on the CPU (gloo): the exchange of the vocab-sharded top-k and row
-sharding. The kernels' CPU stand-ins here are the oracle's (test infrastructure); the exchange code is the product's
+"""The multi-GPU host path with world_size 2 on the CPU (gloo): the exchange of the vocab-sharded top-k, row
+sharding and RoPE token sharding. The kernels' CPU stand-ins here are the oracle's (test infrastructure); the exchange code is the product's
 (ckb200.sharded.gather_lists)."""
 
 import os
@@ -15,6 +15,19 @@ def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         return s.getsockname()[1]
+
+
+def _gather_tokens(t, sizes):
+    """All-gather of every rank's [1, n_r, ...] token shard (n_r from sizes, which may differ by one): padded to the
+    largest shard for the collective, trimmed after, concatenated along the tokens."""
+    import torch.distributed as dist
+
+    most = max(b - a for a, b in sizes)
+    pad = torch.zeros((1, most, *t.shape[2:]), dtype=t.dtype, device=t.device)
+    pad[:, :t.shape[1]] = t
+    parts = [torch.empty_like(pad) for _ in sizes]
+    dist.all_gather(parts, pad)
+    return torch.cat([p[:, :b - a] for p, (a, b) in zip(parts, sizes)], 1)
 
 
 def _worker(rank, world, port, q):
@@ -46,6 +59,19 @@ def _worker(rank, world, port, q):
         dist.all_gather(spans, span)
         ok_rows = spans[0][0] == 0 and spans[-1][1] == 16384 and all(
             spans[j][1] == spans[j + 1][0] for j in range(world - 1))
+        # token sharding of RoPE: every rank rotates its own tokens (the oracle stands in for the kernel here);
+        # gathered over the ranks they equal the whole batch's rotation
+        from ckb200 import workloads
+        from oracle import rope as orope
+        rp = workloads.rope_8x4096(integer=True, batch=3, seq=101)
+        tq = sharded.token_shard(rp["q"], rank, world)
+        tk = sharded.token_shard(rp["k"], rank, world)
+        ids = sharded.token_shard(rp["position_ids"], rank, world)
+        mq, _ = orope.rope(tq, tk, rp["cos"], rp["sin"], ids)
+        sizes = [sharded.token_range(303, r, world) for r in range(world)]
+        gathered = _gather_tokens(mq.contiguous().view(torch.float16), sizes)  # moved as raw 16-bit words
+        wq, _ = orope.rope(rp["q"], rp["k"], rp["cos"], rp["sin"], rp["position_ids"])
+        ok_rows = ok_rows and torch.equal(gathered.view(torch.int16), wq.view(1, -1, 32, 128).view(torch.int16))
         q.put((rank, bool(ok_topk), bool(ok_rows)))
         dist.destroy_process_group()
     except Exception as e:  # report instead of hanging the parent

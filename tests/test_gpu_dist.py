@@ -2,7 +2,9 @@
   * the vocab-sharded top-k (local shard kernel -> all_gather_into_tensor -> merge kernel) gives every rank the
     single-GPU answer, bit for bit, and so does its peer-memory form (PeerVocabShardedTopK: NVLink stores and
     per-row flags instead of the collective), call after call (both parity halves, fp32 and bf16);
-  * row sharding: each rank normalises its own rows; gathered, they equal the oracle.
+  * row sharding: each rank normalises its own rows; gathered, they equal the oracle;
+  * token sharding: each rank rotates its own tokens of an integer-valued RoPE batch in place (sharded.token_shard,
+    the cos/sin cache replicated); gathered, they equal the oracle bit for bit.
 Ranks are spawned processes with a short process-group timeout, so a stuck collective ends the test with an error."""
 
 import datetime
@@ -22,6 +24,19 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _gather_tokens(t, sizes):
+    """All-gather of every rank's [1, n_r, ...] token shard (n_r from sizes, which may differ by one): padded to the
+    largest shard for the collective, trimmed after, concatenated along the tokens."""
+    import torch.distributed as dist
+
+    most = max(b - a for a, b in sizes)
+    pad = torch.zeros((1, most, *t.shape[2:]), dtype=t.dtype, device=t.device)
+    pad[:, :t.shape[1]] = t
+    parts = [torch.empty_like(pad) for _ in sizes]
+    dist.all_gather(parts, pad)
+    return torch.cat([p[:, :b - a] for p, (a, b) in zip(parts, sizes)], 1)
+
+
 def _worker(rank, world, port, q):
     import sys
 
@@ -30,8 +45,9 @@ def _worker(rank, world, port, q):
     sys.path[:0] = [here, root, os.path.join(root, "cuda-kernels-optimized-for-rtx5090_b200")]
     import torch.distributed as dist
 
-    from ckb200 import rmsnorm, sharded, workloads
+    from ckb200 import rmsnorm, rope, sharded, workloads
     from oracle import rmsnorm as orms
+    from oracle import rope as orope
     from oracle import topk as otk
     from oracle.numerics import to_f32, ulp_distance
 
@@ -61,8 +77,7 @@ def _worker(rank, world, port, q):
             gv, gi = step()
             torch.cuda.synchronize()
             ok_topk = ok_topk and torch.equal(gi.cpu(), wi) and torch.equal(gv.cpu(), wv)
-        from ckb200 import _native
-        ok_topk = ok_topk and _native.load("topk").ckb_topk_status(1) == 0
+        peer.check()  # raises if any peer wait ran out
         peer.close()
         inp = workloads.rmsnorm_16384x4096(scale=64)
         r0, r1 = sharded.row_range(inp["x"].shape[0], rank, world)
@@ -74,6 +89,18 @@ def _worker(rank, world, port, q):
         full = torch.cat(parts).cpu()
         ok_rows = int(ulp_distance(to_f32(full), to_f32(orms.rmsnorm(inp["x"], inp["weight"])),
                                    torch.bfloat16).max()) <= 1
+        # token-sharded RoPE: uneven shards (3 x 999 tokens do not divide by most world sizes)
+        rp = workloads.rope_8x4096(integer=True, batch=3, seq=999)
+        tq = sharded.token_shard(rp["q"], rank, world).to(dev)
+        tk = sharded.token_shard(rp["k"], rank, world).to(dev)
+        ids = sharded.token_shard(rp["position_ids"], rank, world).to(dev)
+        rope.rope(tq, tk, ids, rp["cos"].to(dev), rp["sin"].to(dev), inplace=True)
+        sizes = [sharded.token_range(3 * 999, r, world) for r in range(world)]
+        gq = _gather_tokens(tq, sizes).cpu().view(torch.int16)
+        gk = _gather_tokens(tk, sizes).cpu().view(torch.int16)
+        wq, wk = orope.rope(rp["q"], rp["k"], rp["cos"], rp["sin"], rp["position_ids"])
+        ok_rows = ok_rows and torch.equal(gq, wq.view(1, -1, 32, 128).view(torch.int16)) and \
+            torch.equal(gk, wk.view(1, -1, 8, 128).view(torch.int16))
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, bool(ok_topk), bool(ok_rows)))
