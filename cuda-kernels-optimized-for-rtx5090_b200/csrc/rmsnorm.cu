@@ -11,7 +11,8 @@
 // B200 mapping (HBM bound: 2 bytes read + 2 written per element, the weight stays in L1/L2):
 //   * rows of at most 128 16-byte vectors: one warp per row, 8 rows per 256-thread block, no block barrier;
 //   * rows of at most 4096 vectors: one block per row, each thread keeps VPT 16-byte vectors in registers
-//     (VPT = 1..8, chosen so a block has about 128 threads); one barrier per row;
+//     (VPT = 1..8, chosen so a block has about 256 threads, 128 with a weight) and the weight's vectors for the same
+//     columns, fetched with the row's loads so no weight load waits behind the reduction; one barrier per row;
 //   * anything else (cols % 8 != 0, a pointer not 16-byte aligned, longer rows): a scalar block-per-row kernel that
 //     reads the row twice.
 #include "ckb200_rmsnorm.h"
@@ -25,19 +26,31 @@ namespace {
 
 struct NoWeight {};
 
-// The weight of 8 consecutive columns starting at element i as fp32 (i is a multiple of 8, w 16-byte aligned).
-__device__ __forceinline__ void load_w8(const NoWeight*, long long, float (&)[8]) {}
-__device__ __forceinline__ void load_w8(const float* w, long long i, float (&f)[8]) {
-  const float4 a = __ldg(reinterpret_cast<const float4*>(w + i));
-  const float4 b = __ldg(reinterpret_cast<const float4*>(w + i) + 1);
-  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-  f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+// The weight of 8 consecutive columns starting at element i (a multiple of 8, w 16-byte aligned), fetched raw so the
+// load can be issued with the row's own loads and widened to fp32 only where it is used.
+struct NoW8 {};
+struct W8x16 { uint4 r; };
+struct W8x32 { float4 a, b; };
+template <typename WT> struct WRaw { using type = W8x16; };
+template <> struct WRaw<NoWeight> { using type = NoW8; };
+template <> struct WRaw<float> { using type = W8x32; };
+
+__device__ __forceinline__ NoW8 fetch_w8(const NoWeight*, long long) { return {}; }
+__device__ __forceinline__ W8x32 fetch_w8(const float* w, long long i) {
+  return {__ldg(reinterpret_cast<const float4*>(w + i)), __ldg(reinterpret_cast<const float4*>(w + i) + 1)};
 }
-__device__ __forceinline__ void load_w8(const __nv_bfloat16* w, long long i, float (&f)[8]) {
-  unpack16(__ldg(reinterpret_cast<const uint4*>(w + i)), f, w);
+template <typename W>
+__device__ __forceinline__ W8x16 fetch_w8(const W* w, long long i) {
+  return {__ldg(reinterpret_cast<const uint4*>(w + i))};
 }
-__device__ __forceinline__ void load_w8(const __half* w, long long i, float (&f)[8]) {
-  unpack16(__ldg(reinterpret_cast<const uint4*>(w + i)), f, w);
+__device__ __forceinline__ void widen_w8(const NoW8&, const NoWeight*, float (&)[8]) {}
+__device__ __forceinline__ void widen_w8(const W8x32& r, const float*, float (&f)[8]) {
+  f[0] = r.a.x; f[1] = r.a.y; f[2] = r.a.z; f[3] = r.a.w;
+  f[4] = r.b.x; f[5] = r.b.y; f[6] = r.b.z; f[7] = r.b.w;
+}
+template <typename W>
+__device__ __forceinline__ void widen_w8(const W8x16& r, const W* w, float (&f)[8]) {
+  unpack16(r.r, f, w);
 }
 
 __device__ __forceinline__ float load_w1(const NoWeight*, long long) { return 1.0f; }
@@ -71,10 +84,16 @@ __global__ void __launch_bounds__(256) rms_warp_rows(const T* __restrict__ x, co
   const T* xr = x + row * cols;
   T* yr = y + row * cols;
   uint4 v[VPT];
+  typename WRaw<WT>::type wr[VPT];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int i = lane + 32 * k;
     v[k] = i < nvec ? ld_stream(xr + 8 * i) : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int i = lane + 32 * k;
+    if (i < nvec) wr[k] = fetch_w8(w, 8LL * i);
   }
   float ss = 0.0f;
 #pragma unroll
@@ -91,7 +110,7 @@ __global__ void __launch_bounds__(256) rms_warp_rows(const T* __restrict__ x, co
     if (i < nvec) {
       float f[8], wf[8];
       unpack16(v[k], f, x);
-      load_w8(w, 8LL * i, wf);
+      widen_w8(wr[k], w, wf);
       scale8<kW>(f, inv, wf);
       st_stream(yr + 8 * i, pack16(f, x));
     }
@@ -109,10 +128,16 @@ __global__ void __launch_bounds__(VPT >= 8 ? 512 : 1024) rms_block_rows(const T*
   const T* xr = x + off;
   T* yr = y + off;
   uint4 v[VPT];
+  typename WRaw<WT>::type wr[VPT];
 #pragma unroll
   for (int k = 0; k < VPT; ++k) {
     const int i = threadIdx.x + k * blockDim.x;
     v[k] = i < nvec ? ld_stream(xr + 8 * i) : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {  // the weight's loads go out with the row's, off the row's critical path
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i < nvec) wr[k] = fetch_w8(w, 8LL * i);
   }
   float ss = 0.0f;
 #pragma unroll
@@ -136,7 +161,7 @@ __global__ void __launch_bounds__(VPT >= 8 ? 512 : 1024) rms_block_rows(const T*
     if (i < nvec) {
       float f[8], wf[8];
       unpack16(v[k], f, x);
-      load_w8(w, 8LL * i, wf);
+      widen_w8(wr[k], w, wf);
       scale8<kW>(f, inv, wf);
       st_stream(yr + 8 * i, pack16(f, x));
     }
@@ -170,11 +195,15 @@ __global__ void __launch_bounds__(1024) rms_generic(const T* __restrict__ x, con
 
 constexpr int kWarpRowsMaxVec = 128;      // warp path: at most 4 vectors per lane
 constexpr int kBlockRowsMaxVec = 4096;    // block path: at most 512 threads x 8 vectors
+// Block path: VPT grows until a row needs at most this many threads. Measured on B200 at 16384 x 4096 bf16 (and
+// 2048 rows): without a weight 256 threads (2 vectors each) are fastest, with one 128 threads (4 vectors and the
+// weight's 4, more registers per thread but fewer, fuller CTAs).
 #ifndef CKB_RMSNORM_TARGET_THREADS
-#define CKB_RMSNORM_TARGET_THREADS 128
+#define CKB_RMSNORM_TARGET_THREADS 256
 #endif
-constexpr int kBlockTargetThreads = CKB_RMSNORM_TARGET_THREADS;  // block path: VPT grows until a row needs at most
-                                                                 // this many threads
+#ifndef CKB_RMSNORM_TARGET_THREADS_W
+#define CKB_RMSNORM_TARGET_THREADS_W 128
+#endif
 
 template <typename T, typename WT, int VPT>
 void start_warp(const void* x, const void* w, void* y, long long rows, int cols, float eps, cudaStream_t s) {
@@ -200,8 +229,10 @@ int dispatch(const void* x, const void* w, void* y, long long rows, int cols, fl
     return (int)cudaGetLastError();
   }
   if (vec && nvec <= kBlockRowsMaxVec) {
+    constexpr int target = std::is_same<WT, NoWeight>::value ? CKB_RMSNORM_TARGET_THREADS
+                                                             : CKB_RMSNORM_TARGET_THREADS_W;
     int vpt = 1;
-    while (vpt < 8 && (nvec + vpt - 1) / vpt > kBlockTargetThreads) vpt *= 2;
+    while (vpt < 8 && (nvec + vpt - 1) / vpt > target) vpt *= 2;
     const int threads = ((nvec + vpt - 1) / vpt + 31) / 32 * 32;
     switch (vpt) {
       case 1: start_block<T, WT, 1>(x, w, y, rows, cols, threads, eps, s); break;
