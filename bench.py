@@ -232,7 +232,7 @@ def workload_bytes(name, rows):
     raise SystemExit(f"unknown workload {name}")
 
 
-def make_case(name, impl="ours", seeded=True, rows=None):
+def make_case(name, impl="ours", seeded=True, rows=None, kind="randn"):
     """Device buffers for workload `name`, `rows` rows of it (tokens for RoPE; default the full config), rotated over
     enough buffer sets to defeat the L2. seeded: the workloads module's CPU-seeded inputs (checkable against the
     oracle; full config only); otherwise the same distributions drawn on the device (faster to make)."""
@@ -353,7 +353,14 @@ def make_case(name, impl="ours", seeded=True, rows=None):
         return Case(name, nbytes, rows, launch, sets, None, "rope_tokens")
 
     if name == "topk_512x151936":
-        x0 = workloads.topk_512x151936()["x"].to(dev) if seeded else dev_randn(rows, 151936, scale=3.0)
+        if kind == "ascending":  # every tile beats the running top k: the overflow path on every tile
+            x0 = torch.arange(151936, device=dev, dtype=torch.float32).repeat(rows, 1) + dev_randn(rows, 1)
+        elif kind == "descending":  # the row's top k all in its first tile: the speculative bound fails, two passes
+            x0 = -torch.arange(151936, device=dev, dtype=torch.float32).repeat(rows, 1)
+        elif kind == "fewvalued":  # 8 distinct values: massive ties, resolved by index
+            x0 = torch.randint(0, 8, (rows, 151936), generator=g, device=dev).float()
+        else:
+            x0 = workloads.topk_512x151936()["x"].to(dev) if seeded else dev_randn(rows, 151936, scale=3.0)
         xs = [x0] + [x0.clone() for _ in range(sets - 1)]
         lib = _lib("topk") if impl == "ours" else _ref_lib("topk")
         if lib is None:
@@ -795,6 +802,22 @@ def sweep(args, world):
                 entry[impl]["check"] = bool(case.check())
             del case
             torch.cuda.empty_cache()
+        if name == "topk_512x151936":
+            # data-dependent paths of the streaming top-k, timed beside the reference's kernel on the same rows
+            adv = {}
+            for kind in ("ascending", "descending", "fewvalued"):
+                adv[kind] = {}
+                for impl in ("ours", "ref"):
+                    case = make_case(name, impl=impl, seeded=False, kind=kind)
+                    if case is None:
+                        continue
+                    ms, _ = time_case(case, 50, 5, world)
+                    adv[kind][impl] = {"us": round(ms / 50 * 1e3, 2)}
+                    if impl == "ours":
+                        adv[kind][impl]["check"] = bool(case.check())
+                    del case
+                    torch.cuda.empty_cache()
+            entry["adversarial_rows"] = adv
         entry["e2e"] = time_e2e(name, max(3, args.e2e_steps // 2), 2, world)
         torch.cuda.empty_cache()
         if not args.no_cpu:

@@ -69,6 +69,12 @@ typedef unsigned long long u64;
 #ifndef CKB_TOPK_SLOTS_256H
 #define CKB_TOPK_SLOTS_256H 32
 #endif
+#ifndef CKB_TOPK_STRICT
+#define CKB_TOPK_STRICT 1
+#endif
+#ifndef CKB_TOPK_OVF_BOUND
+#define CKB_TOPK_OVF_BOUND 1
+#endif
 #ifndef CKB_TOPK_WIDE_ONLY
 #define CKB_TOPK_WIDE_ONLY 0
 #endif
@@ -577,13 +583,6 @@ __device__ int compact(u64* cand, int np, int n, int k, u64* tmp, unsigned* warp
   return min(k, n);
 }
 
-// The bound after a compaction that left a full top k: one above its k-th entry (every composite that can still
-// enter is larger), never below the bound already in force.
-__device__ __forceinline__ u64 raise_bound(u64 lo, u64 kth) {
-  const u64 b = kth == ~0ull ? kth : kth + 1ull;
-  return b > lo ? b : lo;
-}
-
 constexpr int kMaxPeers = 8;
 
 // Modes 2 and 3 (vocab-sharded top-k over peer memory): each rank's exchange buffer holds, for the current call's
@@ -682,6 +681,58 @@ __device__ __forceinline__ void publish_row(const SegArgs& a, long long row, int
   if (tid < a.k) __threadfence_system();
   __syncthreads();
   if (tid < a.push.world) st_release_sys(a.push.flags[tid] + (long long)a.push.rank * a.push.rows + row, a.push.epoch);
+}
+
+// The end of a segment: its sorted top k (cand[0, k), zero padded) becomes the row's output in the launch's mode, or,
+// for a row split into several segments, goes to the workspace, and the row's last CTA (per-row counter, reset by it)
+// merges the segments' lists in `scratch` (two halves of merge_entries composites, idle shared memory) and writes
+// the output. All threads of the CTA call it.
+template <typename T>
+__device__ void finish_segment(const SegArgs& a, long long row, int seg, int nseg, const u64* cand, int k,
+                               unsigned char* scratch, int merge_entries, int* s_last, int* s_timeout) {
+  const int tid = threadIdx.x, nthreads = blockDim.x;
+  if (nseg == 1) {
+    for (int i = tid; i < k; i += nthreads) emit<T>(a, row, i, cand[i]);
+    if (a.mode >= 2) publish_row(a, row, tid);
+    if (a.mode == 3) merge_published<T>(a, row, tid, nthreads, reinterpret_cast<u64*>(scratch), s_timeout);
+    return;
+  }
+  u64* wr = a.work + ((long long)row * nseg + seg) * k;
+  // The writers (threads below k <= nthreads) fence their own stores before the row counter moves.
+  if (tid < k) {
+    wr[tid] = cand[tid];
+    __threadfence();
+  }
+  __syncthreads();
+  if (tid == 0) *s_last = atomicAdd(&a.counters[row], 1u) == (unsigned)nseg - 1u;
+  __syncthreads();
+  if (!*s_last) return;
+  __threadfence();
+  u64* la = reinterpret_cast<u64*>(scratch);  // the ring is idle: two halves of nseg * k <= merge_entries each
+  u64* lb = la + merge_entries;
+  const u64* rw = a.work + (long long)row * nseg * k;
+  for (int i = tid; i < nseg * k; i += nthreads) la[i] = __ldcg(rw + i);
+  __syncthreads();
+  // Pairwise rounds: lists 2p and 2p + 1 become list p (an odd last list moves on as it is). An entry's place in the
+  // merged list is its place in its own list plus the entries of the partner list above it; zero padding lands
+  // behind every real entry.
+  for (int n = nseg; n > 1; n = (n + 1) / 2) {
+    for (int i = tid; i < n * k; i += nthreads) {
+      const int l = i / k, e = i - l * k;
+      const u64 c = la[i];
+      int rank = e;
+      if (!((n & 1) && l == n - 1)) rank += count_greater(la + (l ^ 1) * k, k, c);
+      if (rank < k) lb[(l >> 1) * k + rank] = c;
+    }
+    __syncthreads();
+    u64* sw = la;
+    la = lb;
+    lb = sw;
+  }
+  for (int i = tid; i < k; i += nthreads) emit<T>(a, row, i, la[i]);
+  if (tid == 0) a.counters[row] = 0u;
+  if (a.mode >= 2) publish_row(a, row, tid);  // its barrier also ends every read of la / lb in the ring
+  if (a.mode == 3) merge_published<T>(a, row, tid, nthreads, reinterpret_cast<u64*>(scratch), s_timeout);
 }
 
 // Grid (nseg, rows). A row's 16-byte aligned body is split evenly into nseg segments of vectors; the elements before
@@ -789,6 +840,22 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   u64 lo = 0;      // every composite that can still enter the top k (or, speculating, pass the check) is >= lo
   u64 spec = 0;    // the highest speculative bound used
   bool speculate = true;
+  // lo is an element's own composite (or one above it, within the same key): an element not yet streamed has a larger
+  // index, so one of equal value falls below lo and the float pre-filter of later tiles may drop equal values.
+  bool lo_strict = false;
+  auto set_lo = [&](u64 v, bool strict) {
+    if (v > lo) {
+      lo = v;
+      lo_strict = strict;
+    } else if (v == lo && strict) {
+      lo_strict = true;
+    }
+  };
+  // The bound after a compaction that left a full top k: one above its k-th entry (strict unless the +1 carries into
+  // the key, which happens only for index 0).
+  auto raise_to = [&](u64 kth) {
+    if (kth != ~0ull) set_lo(kth + 1ull, (unsigned)kth != 0xffffffffu);
+  };
 
   // Appends the current collect's or expansion's count (all threads call it, after the appends and a barrier).
   auto take_count = [&]() {
@@ -801,13 +868,13 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
     ntop = compact<NT>(cand, ntop, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
     filled = 0;
     if (ntop == k) {
-      lo = raise_bound(lo, cand[k - 1]);
+      raise_to(cand[k - 1]);
       if (speculate && seen >= 0.0f) {
         const int m = spec_rank(k, seen);
         if (m < k) {
           const u64 s_m = cand[m - 1];
           spec = s_m > spec ? s_m : spec;
-          lo = s_m > lo ? s_m : lo;
+          set_lo(s_m, true);
         }
       }
     }
@@ -823,10 +890,10 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
       __syncthreads();  // every thread has read s_cnt
       ntop = compact<NT>(cand, ntop, ntop + filled, k, tmp, warp_tot, &s_bin, &s_above, &s_pack);
       filled = 0;
-      if (ntop == k) lo = raise_bound(lo, cand[k - 1]);
+      if (ntop == k) raise_to(cand[k - 1]);
       const u64 edge = radix_edge<NT>([&](auto&& f) { for_each_at_least(t, lo, f); }, (unsigned)k, kCand - ntop,
                                   reinterpret_cast<unsigned*>(tmp), warp_tot, &s_bin, &s_above);
-      lo = edge > lo ? edge : lo;
+      set_lo(edge, false);
       if (tid == 0) s_cnt = 0;
       __syncthreads();
       collect(t, lo, cand, ntop, &s_cnt);
@@ -858,13 +925,51 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
       const u64 edge = radix_edge<NT>(
           [&](auto&& f) { for_each_recorded<T>(wslot, widx, n, t.base_idx, lo, f); }, (unsigned)k, kCand - ntop,
           reinterpret_cast<unsigned*>(tmp), warp_tot, &s_bin, &s_above);
-      lo = edge > lo ? edge : lo;
+      set_lo(edge, false);
     }
     if (tid == 0) s_cnt = 0;
     __syncthreads();
     expand<T, kCand>(wslot, widx, n, t.base_idx, lo, cand, ntop + filled, &s_cnt);
     __syncthreads();
     take_count();
+  };
+
+  // The c-th largest per-thread maximum of each warp over the tile in registers (and the extra element), smallest over
+  // the warps, as a key: c * warps elements of the tile are at or above it. Key 0 (no number's key) when a warp holds
+  // fewer than c numbers: no bound. All threads call it; it ends with a barrier.
+  auto tile_bound = [&](int c) -> unsigned {
+    float fm = __int_as_float(0x7fc00000);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) fm = vec_max(t.r[u], fm, tag);
+    if (t.has_x) fm = max3(fm, __uint_as_float(t.xbits), __uint_as_float(t.xbits));
+    // A bitonic sort of the 32 keys across the lanes, descending: lane l ends with the (l + 1)-th largest.
+    unsigned key = fm == fm ? order_key(__float_as_uint(fm)) : 0u;
+#pragma unroll
+    for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        const unsigned o = __shfl_xor_sync(0xffffffffu, key, stride);
+        const bool keep_max = ((lane & stride) == 0) == ((lane & size) == 0);
+        key = keep_max ? max(key, o) : min(key, o);
+      }
+    }
+    const unsigned wk = __shfl_sync(0xffffffffu, key, c - 1);
+    if (lane == 0) warp_key[warp] = wk;
+    __syncthreads();
+    unsigned b = warp_key[0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) b = min(b, warp_key[w]);
+    return b;
+  };
+  // The float pre-filter of later tiles for the bound lo: the value of lo's key, or, when lo is strict, the next float
+  // above it (equal values cannot pass; -0 keeps the plain form, since +0 compares equal to it as a float but ranks
+  // above it).
+  auto prefilter = [&]() {
+    const unsigned kb = key_bits((unsigned)(lo >> 32));
+    float f = __uint_as_float(kb);
+    if (CKB_TOPK_STRICT && lo_strict && kb != 0x80000000u && f == f && f != CUDART_INF_F)
+      f = __uint_as_float((kb & 0x80000000u) ? kb - 1u : kb + 1u);
+    return f;
   };
 
   for (int pass = 0; pass < 2; ++pass) {
@@ -879,36 +984,13 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
     spec = 0;
 
     // Tile 0: the bound, every composite at or above it, and a first compaction that sets the running bounds.
+    const int c_full = (k + kWarps - 1) / kWarps;
     issue(kStages - 1, kStages - 1);
     cp_async_wait<kStages - 1>();
     load(0, 0);
     t.has_x = mine_x;
-    {
-      // The c-th largest per-thread maximum of each warp (key 0 when a thread saw no number), smallest over the
-      // warps. Key 0 is no number's key, so a warp short of c numbers leaves the bound at 0: no bound.
-      float fm = __int_as_float(0x7fc00000);
-#pragma unroll
-      for (int u = 0; u < kU; ++u) fm = vec_max(t.r[u], fm, tag);
-      if (t.has_x) fm = max3(fm, __uint_as_float(t.xbits), __uint_as_float(t.xbits));
-      // A bitonic sort of the 32 keys across the lanes, descending: lane l ends with the (l + 1)-th largest.
-      unsigned key = fm == fm ? order_key(__float_as_uint(fm)) : 0u;
-#pragma unroll
-      for (int size = 2; size <= 32; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-          const unsigned o = __shfl_xor_sync(0xffffffffu, key, stride);
-          const bool keep_max = ((lane & stride) == 0) == ((lane & size) == 0);
-          key = keep_max ? max(key, o) : min(key, o);
-        }
-      }
-      const unsigned wk = __shfl_sync(0xffffffffu, key, (k + kWarps - 1) / kWarps - 1);
-      if (lane == 0) warp_key[warp] = wk;
-      __syncthreads();
-      unsigned b = warp_key[0];
-#pragma unroll
-      for (int w = 1; w < kWarps; ++w) b = min(b, warp_key[w]);
-      lo = (u64)b << 32;
-    }
+    lo = (u64)tile_bound(c_full) << 32;
+    lo_strict = false;
     collect_tile();
     compact_all(seen_after(0));
     t.has_x = false;
@@ -917,7 +999,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
     int wcnt = 0;                           // this warp's recorded vectors
     int rs = kStages > 1 ? 1 % kStages : 0;  // ring stage of tile j
     int fs = 1;                             // s_flag word of tile j
-    float f_lo = __uint_as_float(key_bits((unsigned)(lo >> 32)));
+    float f_lo = prefilter();
     for (int j = 1; j < ntiles; ++j) {
       issue(j + kStages - 1, rs == 0 ? kStages - 1 : rs - 1);  // into the stage tile j - 1 left
       cp_async_wait<kStages - 1>();                            // this thread's copies of tile j have landed
@@ -930,17 +1012,20 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
       __syncthreads();
       const int flag = s_flag[fs];
       if (flag & 2) {
-        // Some warp overflowed: keep every warp's records from earlier tiles, take this tile from registers.
+        // Some warp overflowed: keep every warp's records from earlier tiles, take this tile from registers, after
+        // raising the bound to the tile's own guaranteed bound (k of its elements are at or above it), so a tile of
+        // rising values collects about k composites instead of all of them.
         expand_all(before);
         wcnt = 0;
+        if (CKB_TOPK_OVF_BOUND) set_lo((u64)tile_bound(c_full) << 32, false);
         collect_tile();
         compact_all(seen_after(j));
-        f_lo = __uint_as_float(key_bits((unsigned)(lo >> 32)));
+        f_lo = prefilter();
       } else if (flag & 1) {
         expand_all(wcnt);
         wcnt = 0;
         if (filled > 0) compact_all(seen_after(j));
-        f_lo = __uint_as_float(key_bits((unsigned)(lo >> 32)));
+        f_lo = prefilter();
       }
       rs = rs + 1 == kStages ? 0 : rs + 1;
       fs = fnext;
@@ -952,50 +1037,9 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
     __syncthreads();  // every thread has read cand[k - 1] before the second pass clears the buffer
   }
 
-  // Output, or the multi-segment merge by the row's last CTA.
-  if (nseg == 1) {
-    for (int i = tid; i < k; i += kThreads) emit<T>(a, row, i, cand[i]);
-    if (a.mode >= 2) publish_row(a, row, tid);
-    if (a.mode == 3) merge_published<T>(a, row, tid, kThreads, reinterpret_cast<u64*>(smem_raw), &s_timeout);
-    return;
-  }
-  u64* wr = a.work + ((long long)row * nseg + seg) * k;
-  // The writers (threads below k <= kThreads) fence their own stores before the row counter moves.
-  if (tid < k) {
-    wr[tid] = cand[tid];
-    __threadfence();
-  }
-  __syncthreads();
-  if (tid == 0) s_last = atomicAdd(&a.counters[row], 1u) == (unsigned)nseg - 1u;
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  u64* la = reinterpret_cast<u64*>(smem_raw);  // the ring is idle: two halves of nseg * k <= kMergeEntries each
-  u64* lb = la + kMergeEntries;
-  const u64* rw = a.work + (long long)row * nseg * k;
-  for (int i = tid; i < nseg * k; i += kThreads) la[i] = __ldcg(rw + i);
-  __syncthreads();
-  // Pairwise rounds: lists 2p and 2p + 1 become list p (an odd last list moves on as it is). An entry's place in the
-  // merged list is its place in its own list plus the entries of the partner list above it; zero padding lands
-  // behind every real entry.
-  for (int n = nseg; n > 1; n = (n + 1) / 2) {
-    for (int i = tid; i < n * k; i += kThreads) {
-      const int l = i / k, e = i - l * k;
-      const u64 c = la[i];
-      int rank = e;
-      if (!((n & 1) && l == n - 1)) rank += count_greater(la + (l ^ 1) * k, k, c);
-      if (rank < k) lb[(l >> 1) * k + rank] = c;
-    }
-    __syncthreads();
-    u64* sw = la;
-    la = lb;
-    lb = sw;
-  }
-  for (int i = tid; i < k; i += kThreads) emit<T>(a, row, i, la[i]);
-  if (tid == 0) a.counters[row] = 0u;
-  if (a.mode >= 2) publish_row(a, row, tid);  // its barrier also ends every read of la / lb in the ring
-  if (a.mode == 3) merge_published<T>(a, row, tid, kThreads, reinterpret_cast<u64*>(smem_raw), &s_timeout);
+  finish_segment<T>(a, row, seg, nseg, cand, k, smem_raw, kMergeEntries, &s_last, &s_timeout);
 }
+
 
 // Merge of nlists sorted composite lists per row, lists laid out [nlists][rows][k] (an all-gather's output); one
 // CTA per row writes the top k values and indices.
