@@ -652,6 +652,7 @@ def main():
     if world == 1 and not args.no_sweep:
         line["kernels"] = sweep(args, world)
         line["latency"] = latency()
+        line["fusions"] = fusions()
     if not args.no_multi:
         line["strong"] = strong(args, rank, world)
         line["vocab_topk"] = vocab_topk(args, rank, world, local)
@@ -826,6 +827,69 @@ def sweep(args, world):
     return out
 
 
+def _time_fn(fn, steps=50, warmup=5):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps * 1e3
+
+
+def fusions():
+    """The two fusions at the BASELINE shapes, each beside the unfused steps it replaces (device time per call):
+    RoPE + paged KV-cache write on the RoPE config (q in place, k and v into a 2048 x 16-slot cache, k not written
+    back) against this library's RoPE followed by the cache rows copied in by indexing; top-k sampling (softmax over
+    the 50 largest of each [512, 151936] row, one sampled token per row) against a full-row softmax, the top-k of
+    the probabilities and a renormalisation."""
+    from ckb200 import rope, softmax, topk, workloads
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    g = torch.Generator(device=dev).manual_seed(9)
+    out = {}
+    q = torch.randn(8, 4096, 32, 128, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(8, 4096, 8, 128, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(8, 4096, 8, 128, generator=g, device=dev).to(torch.bfloat16)
+    c, s_ = workloads._rope_cache(10000.0, 128, 4096, torch.float32)
+    cos, sin = c.to(dev), s_.to(dev)
+    ids = torch.arange(4096, device=dev).repeat(8, 1)
+    slots = torch.randperm(32768, generator=g, device=dev).view(8, 4096)
+    kc = torch.empty(2048, 16, 8, 128, dtype=torch.bfloat16, device=dev)
+    vc = torch.empty_like(kc)
+    fused = _time_fn(lambda: rope.rope_kv_cache(q, k, v, ids, cos, sin, kc, vc, slots, write_k=False))
+    flat = slots.view(-1)
+
+    def unfused():
+        rope.rope(q, k, ids, cos, sin, inplace=True)
+        kc.view(-1, 8, 128).index_copy_(0, flat, k.view(-1, 8, 128))
+        vc.view(-1, 8, 128).index_copy_(0, flat, v.view(-1, 8, 128))
+
+    plain = _time_fn(unfused)
+    nbytes = 2 * q.numel() * 2 + 2 * (k.numel() + v.numel()) * 2 + 2 * cos.numel() * 4 + 2 * ids.numel() * 8
+    out["rope_kv_cache_8x4096"] = {"fused_us": round(fused, 2), "unfused_us": round(plain, 2),
+                                   "fused_GB/s": round(nbytes / (fused * 1e-6) / 1e9, 1),
+                                   "unfused": "rope in place, then index_copy_ of k and v into the cache"}
+    del q, k, v, kc, vc
+    x = torch.randn(512, 151936, generator=g, device=dev) * 3
+    u = torch.rand(512, generator=g, device=dev)
+    fused = _time_fn(lambda: topk.topk_softmax(x, 50, temperature=0.8, uniforms=u))
+
+    def unfused_tk():
+        p = softmax.softmax(x / 0.8)
+        vals, idx = topk.topk(p, 50)
+        return vals / vals.sum(-1, keepdim=True), idx
+
+    plain = _time_fn(unfused_tk)
+    out["topk_softmax_512x151936"] = {"fused_us": round(fused, 2), "unfused_us": round(plain, 2),
+                                      "fused_GB/s": round(x.numel() * 4 / (fused * 1e-6) / 1e9, 1),
+                                      "unfused": "full-row softmax, top-k of the probabilities, renormalisation"}
+    return out
+
+
 def latency(reps=200, batch=20):
     """Decode-sized calls through the public API: `eager_us` = device time per call of `reps` back-to-back calls
     (host issue included when it is the slower side), `graph_us` = per replay of a CUDA graph holding one call,
@@ -848,6 +912,17 @@ def latency(reps=200, batch=20):
         k = torch.randn(b, 1, 8, 128, generator=g, device=dev).to(torch.bfloat16)
         ids = torch.full((b, 1), 4095, dtype=torch.int64, device=dev)
         calls[f"rope_decode_b{b}_bf16"] = (lambda q=q, k=k, ids=ids: rope.rope(q, k, ids, cos, sin, inplace=True))
+    vq = torch.randn(64, 1, 32, 128, generator=g, device=dev).to(torch.bfloat16)
+    vk = torch.randn(64, 1, 8, 128, generator=g, device=dev).to(torch.bfloat16)
+    vv = torch.randn(64, 1, 8, 128, generator=g, device=dev).to(torch.bfloat16)
+    vids = torch.full((64, 1), 4095, dtype=torch.int64, device=dev)
+    vslots = torch.arange(64, device=dev).view(64, 1) * 16
+    kcache = torch.zeros(256, 16, 8, 128, dtype=torch.bfloat16, device=dev)
+    vcache = torch.zeros_like(kcache)
+    calls["rope_kv_cache_decode_b64_bf16"] = lambda: rope.rope_kv_cache(vq, vk, vv, vids, cos, sin, kcache, vcache,
+                                                                         vslots, write_k=False)
+    us = torch.rand(1, generator=g, device=dev)
+    calls["topk_softmax_sample_1x128256_fp32"] = lambda: topk.topk_softmax(x, 50, uniforms=us)
     out = {}
     for name, fn in calls.items():
         try:

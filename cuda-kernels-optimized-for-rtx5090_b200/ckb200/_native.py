@@ -28,11 +28,13 @@ SIGNATURES = {
     "rope": {
         "launch": (_INT, [_VP] * 7 + [_LL] + [_INT] * 7 + [_VP]),
         "ckb_rope_sincos_launch": (_INT, [_VP] * 6 + [_LL] + [_INT] * 4 + [_VP]),
+        "ckb_rope_kv_cache_launch": (_INT, [_VP] * 11 + [_LL] + [_INT] * 5 + [_VP]),
     },
     "topk": {
         "plan": (_LL, [_LL, _LL, _INT, _INT, _INT, _INT]),
         "launch": (_INT, [_VP] * 5 + [_LL, _LL, _INT, _INT, _INT, _INT, _LL, _VP]),
         "ckb_topk_shard_launch": (_INT, [_VP] * 4 + [_LL, _LL, _LL, _INT, _INT, _LL, _VP]),
+        "ckb_topk_softmax_launch": (_INT, [_VP] * 5 + [_LL, _LL, _INT, _INT, _LL, _FLT, _VP, _VP, _VP]),
         "ckb_topk_merge_launch": (_INT, [_VP, _INT, _VP, _VP, _LL, _INT, _INT, _VP]),
         "ckb_topk_launch_noalloc": (_INT, [_VP, _VP, _VP, _LL, _LL, _INT, _INT, _VP]),
         "ckb_topk_shard_push_launch": (_INT, [_VP] * 5 + [_LL, _LL, _LL, _INT, _INT, _LL, _PVP, _PVP, _INT, _INT,

@@ -109,3 +109,43 @@ def run(inputs):
     q_out, k_out = rope(inputs["q"], inputs["k"], inputs["position_ids"], inputs.get("cos"), inputs.get("sin"),
                         inputs.get("theta"), bool(inputs.get("inplace", False)))
     return {"q_out": q_out, "k_out": k_out}
+
+
+def rope_kv_cache(q, k, v, position_ids, cos, sin, key_cache, value_cache, slot_mapping, inplace=True,
+                  write_k=True):
+    """RoPE fused with the paged KV-cache write, one kernel: q [B, S, Hq, D] and k [B, S, Hkv, D] are rotated by the
+    cos/sin rows that position_ids [B, S] pick (in place when inplace, else into new tensors; k is not written back
+    when write_k is False), and the rotated k and the unrotated v [B, S, Hkv, D] of token (b, s) are stored into
+    key_cache / value_cache [num_blocks, block_size, Hkv, D] (q's dtype) at slot slot_mapping[b, s] (int64,
+    block * block_size + offset; negative: padding, not written). Returns (q_out, k_out or None)."""
+    problem = _problem(q, k, cos, sin, position_ids)
+    if problem:
+        raise ValueError(f"rope candidate: {problem}")
+    if v.shape != k.shape or v.dtype != k.dtype:
+        raise ValueError(f"rope candidate: v {v.dtype} {tuple(v.shape)} must match k {k.dtype} {tuple(k.shape)}")
+    for name, c in (("key_cache", key_cache), ("value_cache", value_cache)):
+        if c.dtype != q.dtype or c.dim() != 4 or tuple(c.shape[2:]) != tuple(k.shape[2:]) or not c.is_contiguous():
+            raise ValueError(f"rope candidate: {name} must be a contiguous [blocks, block_size, {k.shape[2]}, "
+                             f"{k.shape[3]}] tensor of {q.dtype}, got {c.dtype} {tuple(c.shape)}")
+    if slot_mapping.dtype != torch.int64 or tuple(slot_mapping.shape) != tuple(position_ids.shape):
+        raise ValueError(f"rope candidate: slot_mapping must be int64 {tuple(position_ids.shape)}")
+    _native.require_cuda("rope", q, k, v, position_ids, cos, sin, key_cache, value_cache, slot_mapping)
+    if inplace:
+        if not (q.is_contiguous() and k.is_contiguous()):
+            raise ValueError("rope candidate: in-place rotation needs contiguous q and k")
+        q_out, k_out = q, (k if write_k else None)
+    else:
+        q, k = q.contiguous(), k.contiguous()
+        q_out, k_out = torch.empty_like(q), (torch.empty_like(k) if write_k else None)
+    v, ids, slots = v.contiguous(), position_ids.contiguous(), slot_mapping.contiguous()
+    cos, sin = cos.contiguous(), sin.contiguous()
+    batch, seq, q_heads, head_dim = q.shape
+    lib = _native.load("rope")
+    with torch.cuda.device(q.device):
+        err = lib.ckb_rope_kv_cache_launch(q.data_ptr(), k.data_ptr(), v.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                           ids.data_ptr(), slots.data_ptr(), q_out.data_ptr(),
+                                           None if k_out is None else k_out.data_ptr(), key_cache.data_ptr(),
+                                           value_cache.data_ptr(), batch * seq, q_heads, k.shape[2], head_dim,
+                                           _QK[q.dtype], _CACHE[cos.dtype], _native.stream_of(q))
+    _native.check(err)
+    return q_out, k_out

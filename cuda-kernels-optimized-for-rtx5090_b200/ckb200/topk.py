@@ -102,6 +102,37 @@ def run(inputs):
     return {"values": values, "indices": indices}
 
 
+def topk_softmax(x, k=K, temperature=1.0, uniforms=None):
+    """Top-k sampling over each row of x (fp32 or bf16 logits): (probs, indices, samples). probs [rows, k] float is
+    the softmax over the row's k largest logits divided by temperature, in descending order, with their int64
+    indices; with uniforms (float [rows] in [0, 1), on x's device) samples [rows] int64 holds each row's sampled
+    token (the first entry whose cumulative probability exceeds the uniform), else None. One kernel: the softmax
+    runs in the top-k epilogue, so the row is read once."""
+    dtype = _check_x(x, k)
+    if not (float(temperature) > 0.0 and float(temperature) < float("inf")):
+        raise ValueError(f"topk_softmax: temperature must be a positive finite number, got {temperature}")
+    x = x.contiguous()
+    rows, cols = x.shape
+    chunk, work = _plan(x, rows, cols, dtype, k)
+    counters = _row_counters(x.device, rows)
+    probs = torch.empty((rows, k), dtype=torch.float32, device=x.device)
+    indices = torch.empty((rows, k), dtype=torch.int64, device=x.device)
+    samples = None
+    if uniforms is not None:
+        if uniforms.dtype != torch.float32 or uniforms.shape != (rows,) or uniforms.device != x.device:
+            raise ValueError("topk_softmax: uniforms must be float32 [rows] on x's device")
+        uniforms = uniforms.contiguous()
+        samples = torch.empty(rows, dtype=torch.int64, device=x.device)
+    lib = _native.load("topk")
+    with torch.cuda.device(x.device):
+        err = lib.ckb_topk_softmax_launch(x.data_ptr(), probs.data_ptr(), indices.data_ptr(), work.data_ptr(),
+                                          counters.data_ptr(), rows, cols, k, dtype, chunk, float(temperature),
+                                          None if uniforms is None else uniforms.data_ptr(),
+                                          None if samples is None else samples.data_ptr(), _native.stream_of(x))
+    _native.check(err)
+    return probs, indices, samples
+
+
 def shard_lists(x, col_offset, k=K, out=None):
     """Local top-k of a column shard x [rows, cols] holding global columns [col_offset, col_offset + cols): returns
     [rows, k] int64 tensor whose bits are the sorted 64-bit composites (key << 32 | ~global_index), zero padded."""

@@ -608,6 +608,12 @@ struct SegArgs {
   long long col_offset;  // added to every column index
   int cols, k, mode;
   PushArgs push;         // mode 2
+  // Mode 4 (top-k sampling): values is float [rows, k] and receives softmax(top-k values * inv_temp) in rank order;
+  // with uniforms (float [rows], in [0, 1)), samples[row] (int64) is the index of the first entry whose cumulative
+  // probability exceeds uniforms[row].
+  float inv_temp;
+  const float* uniforms;
+  long long* samples;
 };
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
@@ -631,6 +637,56 @@ __device__ __forceinline__ void emit(const SegArgs& a, long long row, int j, u64
     const long long at = ((long long)a.push.rank * a.push.rows + row) * a.k + j;
     for (int p = 0; p < a.push.world; ++p) a.push.lists[p][at] = c;  // NVLink stores to every rank (and itself)
   }
+}
+
+// Mode 4: the row's final top k (sorted composites in shared memory) as probabilities softmax(v * inv_temp) over the
+// k values (fp32, the exponentials taken against the largest, their sum in fp64) with the int64 indices, and the
+// sampled index when the launch has uniforms. The first warp does it (k <= 512: 16 entries per lane at most); an
+// entry past the row's elements (zero padding) has probability 0 and is never sampled.
+template <typename T>
+__device__ void emit_probs(const SegArgs& a, long long row, const u64* list) {
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x, k = a.k;
+  float* probs = reinterpret_cast<float*>(a.values);
+  const u64 c0 = list[0];
+  const float v0 = to_f32(decode_value<T>(c0)) * a.inv_temp;
+  double sum = 0.0;
+  for (int i = lane; i < k; i += 32) {
+    const u64 c = list[i];
+    if (c != 0ull) sum += (double)expf(to_f32(decode_value<T>(c)) * a.inv_temp - v0);
+  }
+  sum = warp_sum(sum);
+  const float inv = (float)(1.0 / sum);
+  for (int i = lane; i < k; i += 32) {
+    const u64 c = list[i];
+    probs[row * k + i] = c != 0ull ? expf(to_f32(decode_value<T>(c)) * a.inv_temp - v0) * inv : 0.0f;
+    a.indices[row * k + i] = c != 0ull ? decode_index(c) : -1;
+  }
+  if (a.uniforms == nullptr || a.samples == nullptr) return;
+  // The first entry whose cumulative probability exceeds u (the last real entry when rounding leaves u above them
+  // all), by a running scan over the lanes' chunks of 32 entries.
+  const double u = (double)a.uniforms[row] * sum;
+  double base = 0.0;
+  long long pick = -1;
+  for (int i0 = 0; i0 < k && pick < 0; i0 += 32) {
+    const int i = i0 + lane;
+    const u64 c = i < k ? list[i] : 0ull;
+    double e = c != 0ull ? (double)expf(to_f32(decode_value<T>(c)) * a.inv_temp - v0) : 0.0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {  // inclusive scan
+      const double y = __shfl_up_sync(0xffffffffu, e, o);
+      if (lane >= o) e += y;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, c != 0ull && base + e > u);
+    if (hit) pick = decode_index(list[i0 + __ffs(hit) - 1]);
+    base += __shfl_sync(0xffffffffu, e, 31);
+  }
+  if (pick < 0) {  // u at or above the total after rounding: the last real entry
+    int last = k - 1;
+    while (last > 0 && list[last] == 0ull) --last;
+    pick = decode_index(list[last]);
+  }
+  if (lane == 0) a.samples[row] = pick;
 }
 
 // Mode 3, once the row is published: thread p < world waits (bounded) until rank p's list of the row is in this
@@ -692,6 +748,10 @@ __device__ void finish_segment(const SegArgs& a, long long row, int seg, int nse
                                unsigned char* scratch, int merge_entries, int* s_last, int* s_timeout) {
   const int tid = threadIdx.x, nthreads = blockDim.x;
   if (nseg == 1) {
+    if (a.mode == 4) {
+      emit_probs<T>(a, row, cand);
+      return;
+    }
     for (int i = tid; i < k; i += nthreads) emit<T>(a, row, i, cand[i]);
     if (a.mode >= 2) publish_row(a, row, tid);
     if (a.mode == 3) merge_published<T>(a, row, tid, nthreads, reinterpret_cast<u64*>(scratch), s_timeout);
@@ -729,7 +789,9 @@ __device__ void finish_segment(const SegArgs& a, long long row, int seg, int nse
     la = lb;
     lb = sw;
   }
-  for (int i = tid; i < k; i += nthreads) emit<T>(a, row, i, la[i]);
+  if (a.mode == 4) emit_probs<T>(a, row, la);
+  else
+    for (int i = tid; i < k; i += nthreads) emit<T>(a, row, i, la[i]);
   if (tid == 0) a.counters[row] = 0u;
   if (a.mode >= 2) publish_row(a, row, tid);  // its barrier also ends every read of la / lb in the ring
   if (a.mode == 3) merge_published<T>(a, row, tid, nthreads, reinterpret_cast<u64*>(scratch), s_timeout);
@@ -1235,6 +1297,30 @@ CKB_EXPORT int launch(const void* x, void* values, void* indices, void* work, vo
   if (bad_args(x, rows, cols, k, chunk, elem)) return -1;
   if (chunk > cols) chunk = cols;
   const SegArgs a{x, values, (long long*)indices, nullptr, (u64*)work, (unsigned*)counters, 0, (int)cols, k, 0};
+  if (dtype == kF32) return start_seg<float>(a, rows, segments(cols, chunk), stream);
+  return start_seg<__nv_bfloat16>(a, rows, segments(cols, chunk), stream);
+}
+
+// Top-k sampling (no counterpart in the reference): the top k of each row as launch() finds them, then the softmax
+// over those k logits divided by `temperature` (probs float [rows, k], rank order) with their int64 indices, and with
+// uniforms (float [rows], each in [0, 1)) the sampled token of each row into samples (int64 [rows]). work, counters
+// and chunk as in launch() (chunk from plan()). Returns 0, -1 for a rejected argument (launch()'s, a temperature
+// that is not a positive finite number, or only one of uniforms / samples), or the launch's cudaError_t.
+CKB_EXPORT int ckb_topk_softmax_launch(const void* x, float* probs, long long* indices, void* work, void* counters,
+                                       long long rows, long long cols, int k, int dtype, long long chunk,
+                                       float temperature, const float* uniforms, long long* samples,
+                                       cudaStream_t stream) {
+  if (rows <= 0 || k <= 0) return 0;
+  if (dtype != kF32 && dtype != kBF16) return -1;
+  if (!(temperature > 0.0f) || !(temperature < INFINITY) || (uniforms == nullptr) != (samples == nullptr)) return -1;
+  if (probs == nullptr || indices == nullptr) return -1;
+  const int elem = dtype == kBF16 ? 2 : 4;
+  if (bad_args(x, rows, cols, k, chunk, elem)) return -1;
+  if (chunk > cols) chunk = cols;
+  SegArgs a{x, probs, indices, nullptr, (u64*)work, (unsigned*)counters, 0, (int)cols, k, 4};
+  a.inv_temp = 1.0f / temperature;
+  a.uniforms = uniforms;
+  a.samples = samples;
   if (dtype == kF32) return start_seg<float>(a, rows, segments(cols, chunk), stream);
   return start_seg<__nv_bfloat16>(a, rows, segments(cols, chunk), stream);
 }

@@ -24,6 +24,17 @@ int ckb_rope_sincos_launch(const void* q, const void* k, const float* inv_freq, 
                            void* k_out, long long tokens, int q_heads, int kv_heads, int head_dim, int qk_dtype,
                            cudaStream_t stream);
 
+/* RoPE fused with the paged KV-cache write: q and k rotated as launch() does (q_out == q rotates q in place; k_out == k
+ * rotates k in place, k_out null leaves k untouched), and for each token t with slots[t] >= 0 the rotated k and the
+ * unrotated v [tokens, kv_heads, head_dim] (qk_dtype) are stored into key_cache / value_cache [num_blocks,
+ * block_size, kv_heads, head_dim] at row slots[t] (int64; slot = block * block_size + offset; negative: a padding
+ * token, no cache row written). One pass: k and v are read once. No counterpart in the reference, whose RoPE rotates
+ * q and k only (rope/kernel.cu:1-13); the cache layout is the usual paged one (flattened [slot, head, dim]). */
+int ckb_rope_kv_cache_launch(const void* q, const void* k, const void* v, const void* cos_rows, const void* sin_rows,
+                             const void* ids, const void* slots, void* q_out, void* k_out, void* key_cache,
+                             void* value_cache, long long tokens, int q_heads, int kv_heads, int head_dim,
+                             int qk_dtype, int cache_dtype, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -21,6 +21,17 @@ long long plan(long long rows, long long cols, int dtype, int threads, int depth
 int launch(const void* x, void* values, void* indices, void* work, void* counters, long long rows, long long cols,
            int k, int dtype, int threads, int depth, long long chunk, cudaStream_t stream);
 
+/* Top-k sampling: the top k of each row found as launch() does, then probs [rows, k] (float) = the softmax over those k
+ * logits divided by temperature (> 0, finite), in rank order, with their int64 indices [rows, k]; with uniforms
+ * (float [rows], each in [0, 1)) the sampled token of each row, the index of the first entry whose cumulative
+ * probability exceeds the row's uniform, into samples (int64 [rows]); uniforms and samples are both null or both
+ * set. work / counters / chunk as in launch(). No counterpart in the reference (its top-k stops at the values,
+ * topk/kernel.cu:436-441): the softmax over the k survivors runs in the top-k kernel's epilogue, so the vocab row is
+ * read once. */
+int ckb_topk_softmax_launch(const void* x, float* probs, long long* indices, void* work, void* counters,
+                            long long rows, long long cols, int k, int dtype, long long chunk, float temperature,
+                            const float* uniforms, long long* samples, cudaStream_t stream);
+
 /* Vocab-sharded variant, local half: x [rows, cols] holds global columns [col_offset, col_offset + cols); lists
  * [rows, k] receives each row's top k as sorted 64-bit composites (order key << 32 | ~global_index), zero padded.
  * work / counters / chunk as in launch(). No counterpart in the reference (single GPU). */

@@ -57,3 +57,21 @@ def rope_cpu(q, k, cos, sin, position_ids):
         return (xf * c + rh * s).to(x.dtype)
 
     return rot(q), rot(k)
+
+
+def rope_kv_cache(q, k, v, cos, sin, position_ids, key_cache, value_cache, slot_mapping):
+    """Oracle of the fused RoPE + paged KV-cache write (no reference counterpart; its rotation is rope() above):
+    (q_rot, k_rot, key_cache', value_cache') with the rotated k and the unrotated v of token t stored into row
+    slot_mapping[t] of the caches viewed [slots, Hkv, D] (negative slots skipped; other rows unchanged)."""
+    qo, ko = rope(q, k, cos, sin, position_ids)
+    kc = key_cache.detach().cpu().clone()
+    vc = value_cache.detach().cpu().clone()
+    hkv, d = k.shape[2], k.shape[3]
+    kc_rows, vc_rows = kc.view(-1, hkv, d), vc.view(-1, hkv, d)
+    slots = slot_mapping.cpu().reshape(-1)
+    kf, vf = ko.reshape(-1, hkv, d), v.detach().cpu().reshape(-1, hkv, d)
+    for t, sl in enumerate(slots.tolist()):
+        if sl >= 0:
+            kc_rows[sl] = kf[t]
+            vc_rows[sl] = vf[t]
+    return qo, ko, kc, vc

@@ -74,3 +74,21 @@ def topk_cpu(x, k):
     """Multi-threaded torch CPU top-k with the same tie rule (stable descending sort), the timed CPU baseline."""
     v, i = torch.sort(x, dim=-1, descending=True, stable=True)
     return v[:, :k], i[:, :k]
+
+
+def topk_softmax(x, k, temperature=1.0, uniforms=None):
+    """Oracle of top-k sampling (no reference counterpart; its top-k is topk() above): the exact top k, then the
+    softmax of those k logits / temperature in fp64, and for each uniform u the first index whose cumulative
+    probability exceeds u. Returns (probs float64 [rows, k], indices int64 [rows, k], samples int64 [rows] or None,
+    margin: the distance of each u from the nearest cumulative boundary)."""
+    values, indices = topk(x, k)
+    v = values.to(torch.float64) / float(temperature)
+    p = torch.softmax(v, dim=-1)
+    if uniforms is None:
+        return p, indices, None, None
+    cum = torch.cumsum(p, dim=-1)
+    u = uniforms.detach().cpu().to(torch.float64)[:, None]
+    pick = torch.clamp((cum <= u).sum(dim=-1), max=k - 1)
+    samples = indices.gather(1, pick[:, None])[:, 0]
+    margin = (cum - u).abs().min(dim=-1).values
+    return p, indices, samples, margin
