@@ -612,6 +612,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-kernel sweep and latency records")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines (profiling runs)")
     ap.add_argument("--no-multi", action="store_true", help="skip the strong / vocab / rope / host-copy records")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end record (profiling runs)")
     ap.add_argument("--sweep-steps", type=int, default=300)
     ap.add_argument("--e2e-steps", type=int, default=20)
     args = ap.parse_args()
@@ -646,7 +647,8 @@ def main():
                      "traffic": traffic, "traffic_source": traffic_src, "kernel": KERNEL_OF[args.workload]},
         "clocks": clocks, "gpu_launches": args.steps, "check": ok,
     }
-    line["e2e"] = time_e2e(args.workload, args.e2e_steps, 3, world, seeded=True)
+    if not args.no_e2e:
+        line["e2e"] = time_e2e(args.workload, args.e2e_steps, 3, world, seeded=True)
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(args.workload)
     if world == 1 and not args.no_sweep:
@@ -658,9 +660,10 @@ def main():
         line["vocab_topk"] = vocab_topk(args, rank, world, local)
         line["rope_tokens"] = rope_tokens(rank, world)
         hc = host_copy(10, world)
-        hc["e2e_fraction"] = round(line["e2e"]["value"] / world / hc["GB/s_per_rank"] *
-                                   (line["e2e"]["h2d_bytes_per_step"] + line["e2e"]["d2h_bytes_per_step"]) /
-                                   workload_bytes(args.workload, workload_rows(args.workload)), 4)
+        if "e2e" in line:
+            hc["e2e_fraction"] = round(line["e2e"]["value"] / world / hc["GB/s_per_rank"] *
+                                       (line["e2e"]["h2d_bytes_per_step"] + line["e2e"]["d2h_bytes_per_step"]) /
+                                       workload_bytes(args.workload, workload_rows(args.workload)), 4)
         line["host_copy"] = hc
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -138,7 +138,10 @@ struct Cfg {
 template <int NT, int EB>
 constexpr int seg_cap() { return Cfg<NT, EB>::kMergeEntries / Cfg<NT, EB>::kMaxK; }
 constexpr int min2(int a, int b) { return a < b ? a : b; }
-constexpr int kMaxSeg = min2(min2(seg_cap<256, 4>(), seg_cap<256, 2>()), min2(seg_cap<512, 4>(), seg_cap<512, 2>()));
+#ifndef CKB_TOPK_MAX_SEG
+#define CKB_TOPK_MAX_SEG min2(min2(seg_cap<256, 4>(), seg_cap<256, 2>()), min2(seg_cap<512, 4>(), seg_cap<512, 2>()))
+#endif
+constexpr int kMaxSeg = CKB_TOPK_MAX_SEG;
 
 // Radix digits of D bits over the 64-bit composite, most significant first (the last digit takes what is left).
 template <int D>
