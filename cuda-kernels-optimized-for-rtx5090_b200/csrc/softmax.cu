@@ -18,7 +18,8 @@
 //   * stream path (unaligned pointers, cols not a multiple of the vector): one block per row reading the row three
 //     times (max, sum, normalise; the later reads mostly from L2).
 // Accuracy (fp32 outputs within 1e-6 relative of an fp64 softmax, elementwise; outputs below FLT_MIN within two
-// subnormal steps): every path takes 2^64 * exp(x - max) with exp_pair below (relative error within about 2.1e-7).
+// subnormal steps): every path takes 2^64 * exp(x - max) with exp_pair below (relative error within about 2.1e-7);
+// bf16 rows, whose outputs hold 8 bits, take the uncompensated exp_pair_fast (within about 1e-5).
 // Each thread sums its exponentials pairwise per 16-byte vector into an fp64 accumulator, cross-thread and cross-CTA
 // reductions run in fp64, and the output is e * (float)(1 / sum) (or e * (float)(exp(m_c - M) / S) per cluster
 // slice, in two factors when that is below FLT_MIN) with one rounding, so outputs below FLT_MIN are kept as
@@ -109,16 +110,36 @@ __device__ __forceinline__ float2 exp_pair(float2 x, const ExpShift& e) {
   return __ffma2_rn(E, r, E);
 }
 
+// The same scaled exponential for rows of 16-bit values, whose outputs need about 9 good bits, not 24:
+// 2^(s * log2 e + 64) by one ex2.approx (relative error within about 1e-5 for the s of the clamped range: the
+// rounding of the exponent, |s * log2 e| <= 217, dominates), with no compensation. Same 2^64 scale and clamp.
+__device__ __forceinline__ float2 exp_pair_fast(float2 x, const ExpShift& e) {
+  const float2 kL2E = make_float2(1.44269502162933349609375f, 1.44269502162933349609375f);
+  const float2 k64 = make_float2(64.0f, 64.0f);
+  x.x = fmaxf(x.x, e.lowc);
+  x.y = fmaxf(x.y, e.lowc);
+  const float2 t = __ffma2_rn(__fadd2_rn(x, e.nm), kL2E, k64);
+  return make_float2(ex2_ftz(t.x), ex2_ftz(t.y));
+}
+
+// The exponential a row of T takes: compensated for fp32 outputs, plain for 16-bit ones.
+template <typename T>
+__device__ __forceinline__ float2 exp2v(float2 x, const ExpShift& e) {
+  if constexpr (sizeof(T) == 4) return exp_pair(x, e);
+  else return exp_pair_fast(x, e);
+}
+
 // One value (the unaligned stream path): the pair routine with the value in both halves.
-__device__ __forceinline__ float exp_one(float x, const ExpShift& es) { return exp_pair(make_float2(x, x), es).x; }
+template <typename T>
+__device__ __forceinline__ float exp_one(float x, const ExpShift& es) { return exp2v<T>(make_float2(x, x), es).x; }
 
 // In place: f = exp(f - M) by pairs; returns their pairwise sum.
-template <int V>
+template <typename T, int V>
 __device__ __forceinline__ float exp_vec2(float (&f)[V], const ExpShift& es) {
   float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
   for (int j = 0; j < V; j += 2) {
-    const float2 e = exp_pair(make_float2(f[j], f[j + 1]), es);
+    const float2 e = exp2v<T>(make_float2(f[j], f[j + 1]), es);
     f[j] = e.x;
     f[j + 1] = e.y;
     acc = j == 0 ? e : __fadd2_rn(acc, e);
@@ -160,7 +181,7 @@ __global__ void __launch_bounds__(256) sm_group(const T* __restrict__ x, T* __re
   double s = 0.0;
 #pragma unroll
   for (int k = 0; k < NV; ++k)
-    if (in[k]) s += (double)exp_vec2(v[k], es);
+    if (in[k]) s += (double)exp_vec2<T>(v[k], es);
   s = warp_sum<G>(s);
   const float inv = (float)(1.0 / s);
 #pragma unroll
@@ -207,7 +228,7 @@ __global__ void __launch_bounds__(MAXT) sm_block(const T* __restrict__ x, T* __r
   double s = 0.0;
 #pragma unroll
   for (int k = 0; k < NV; ++k)
-    if (in[k]) s += (double)exp_vec2(v[k], es);
+    if (in[k]) s += (double)exp_vec2<T>(v[k], es);
   s = warp_sum(s);
   if (lane == 0) red_s[warp] = s;
   __syncthreads();
@@ -297,7 +318,7 @@ __device__ __forceinline__ void cluster_store(const uint4* buf, uint4* dst, int 
       unpack16(raw, f, (const T*)nullptr);
 #pragma unroll
       for (int j = 0; j < V / 2; ++j) {
-        float2 e = __fmul2_rn(exp_pair(make_float2(f[2 * j], f[2 * j + 1]), es), m1);
+        float2 e = __fmul2_rn(exp2v<T>(make_float2(f[2 * j], f[2 * j + 1]), es), m1);
         if (kTwo) e = __fmul2_rn(e, m2);
         f[2 * j] = e.x;
         f[2 * j + 1] = e.y;
@@ -412,7 +433,7 @@ __global__ void __launch_bounds__(kClusterThreads, 3) sm_cluster(const T* __rest
         unpack16(raw, f, x);
         float2 e[V / 2];
 #pragma unroll
-        for (int j = 0; j < V / 2; ++j) e[j] = exp_pair(make_float2(f[2 * j], f[2 * j + 1]), es);
+        for (int j = 0; j < V / 2; ++j) e[j] = exp2v<T>(make_float2(f[2 * j], f[2 * j + 1]), es);
         const float2 s01 = __fadd2_rn(e[0], e[1]), s23 = __fadd2_rn(e[2], e[3]);
         const float2 s03 = __fadd2_rn(s01, s23);
         sum += (double)(s03.x + s03.y);
@@ -565,9 +586,9 @@ __global__ void __launch_bounds__(kStreamThreads, 2) sm_cluster_stream(const T* 
       for (int u = 0; u < U; ++u) {
         float f[V];
         unpack16(r[u], f, x);
-        float2 acc = exp_pair(make_float2(f[0], f[1]), es);
+        float2 acc = exp2v<T>(make_float2(f[0], f[1]), es);
 #pragma unroll
-        for (int j = 2; j < V; j += 2) acc = __fadd2_rn(acc, exp_pair(make_float2(f[j], f[j + 1]), es));
+        for (int j = 2; j < V; j += 2) acc = __fadd2_rn(acc, exp2v<T>(make_float2(f[j], f[j + 1]), es));
         s += (double)(acc.x + acc.y);
       }
     }
@@ -620,7 +641,7 @@ __global__ void __launch_bounds__(kStreamThreads, 2) sm_cluster_stream(const T* 
         unpack16(r[u], f, x);
 #pragma unroll
         for (int j = 0; j < V; j += 2) {
-          const float2 e = __fmul2_rn(exp_pair(make_float2(f[j], f[j + 1]), es), inv2);
+          const float2 e = __fmul2_rn(exp2v<T>(make_float2(f[j], f[j + 1]), es), inv2);
           f[j] = e.x;
           f[j + 1] = e.y;
         }
@@ -644,10 +665,10 @@ __global__ void __launch_bounds__(1024) sm_stream(const T* __restrict__ x, T* __
   for (long long i = threadIdx.x; i < cols; i += blockDim.x) m = max_nan(m, to_f32(xr[i]));
   const ExpShift es(block_max(m, red));
   double s = 0.0;
-  for (long long i = threadIdx.x; i < cols; i += blockDim.x) s += (double)exp_one(to_f32(xr[i]), es);
+  for (long long i = threadIdx.x; i < cols; i += blockDim.x) s += (double)exp_one<T>(to_f32(xr[i]), es);
   s = block_sum(s, red_d);
   const float inv = (float)(1.0 / s);
-  for (long long i = threadIdx.x; i < cols; i += blockDim.x) yr[i] = from_f32<T>(exp_one(to_f32(xr[i]), es) * inv);
+  for (long long i = threadIdx.x; i < cols; i += blockDim.x) yr[i] = from_f32<T>(exp_one<T>(to_f32(xr[i]), es) * inv);
 }
 
 // ------------------------------------------------------------------------------------------------- dispatch -----
@@ -670,7 +691,10 @@ int start_block(const T* x, T* y, long long rows, int cols, int threads, cudaStr
 }
 
 constexpr long long kMaxRingBytes = 200 * 1024;
-constexpr long long kSliceTarget = 64 * 1024;
+#ifndef CKB_SOFTMAX_SLICE_TARGET
+#define CKB_SOFTMAX_SLICE_TARGET (64 * 1024)
+#endif
+constexpr long long kSliceTarget = CKB_SOFTMAX_SLICE_TARGET;
 
 struct ClusterPlan {
   int cl = 0;         // 0: no cluster configuration fits
