@@ -217,6 +217,8 @@ class Case:
 def workload_bytes(name, rows):
     """Algorithmic bytes of `rows` rows (tokens for RoPE) of workload `name` (the per-launch constants, weight and
     the cos/sin rows read, scale with the rows where they are per-row)."""
+    if name.endswith("_bf16"):
+        return workload_bytes(name[:-5], rows) // 2
     if name == "rmsnorm_16384x4096":
         return 2 * rows * 4096 * 2 + 4096 * 2
     if name == "softmax_4096x8192":
@@ -240,10 +242,14 @@ def make_case(name, impl="ours", seeded=True, rows=None, kind="randn"):
 
     dev = torch.device("cuda", torch.cuda.current_device())
     stream = torch.cuda.current_stream().cuda_stream
+    half = name.endswith("_bf16")  # the softmax configs at bf16 (the reference publishes both dtypes)
+    if half:
+        name = name[:-5]
+        seeded = False
     full_rows = workloads.ROWS[name]
     rows = full_rows if rows is None else rows
     seeded = seeded and rows == full_rows
-    nbytes = workload_bytes(name, rows)
+    nbytes = workload_bytes(name, rows) // (2 if half else 1)
     sets = rotation_sets(nbytes)
     g = torch.Generator(device=dev).manual_seed(1234)
 
@@ -297,7 +303,7 @@ def make_case(name, impl="ours", seeded=True, rows=None, kind="randn"):
             x0 = getattr(workloads, name)()["x"].to(dev)
         else:
             scale = {"softmax_4096x8192": 2.0, "softmax_256x262144": 4.0, "softmax_262144x128": 1.0}[name]
-            x0 = dev_randn(rows, cols, scale=scale)
+            x0 = dev_randn(rows, cols, scale=scale, dtype=torch.bfloat16 if half else torch.float32)
         xs = [x0] + [x0.clone() for _ in range(sets - 1)]
         ys = [torch.empty_like(x0) for _ in range(sets)]
         lib = _lib("softmax") if impl == "ours" else _ref_lib("softmax")
@@ -305,16 +311,21 @@ def make_case(name, impl="ours", seeded=True, rows=None, kind="randn"):
             return None
         lib.launch.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_longlong, ctypes.c_int,
                                ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        code = 1 if half else 0
 
         def launch(i):
-            return lib.launch(xs[i % sets].data_ptr(), ys[i % sets].data_ptr(), rows, cols, 0, 256, 1024, stream)
+            return lib.launch(xs[i % sets].data_ptr(), ys[i % sets].data_ptr(), rows, cols, code, 256, 1024, stream)
 
         def check():
             from oracle import softmax as orc
+            from oracle.numerics import to_f32, ulp_distance
 
             want = orc.softmax_f64(xs[0][:8].cpu())
+            if half:  # within 1 bf16 ulp of the fp64 result rounded
+                return int(ulp_distance(to_f32(ys[0][:8].cpu()), to_f32(want.to(torch.bfloat16)),
+                                        torch.bfloat16).max()) <= 1
             got = ys[0][:8].cpu().double()
-            return bool(((got - want).abs() <= 1e-6 * want.abs()).all())
+            return bool(((got - want).abs() <= torch.clamp(1e-6 * want.abs(), min=2.0 ** -148)).all())
 
         return Case(name, nbytes, rows, launch, sets, check, KERNEL_OF[name])
 
@@ -789,7 +800,7 @@ def sweep(args, world):
     beside them the reference's CPU path at the full config and an end-to-end number through the public API."""
     peak, _ = hbm_peak()
     out = {}
-    for name in ROW_WORKLOADS:
+    for name in ROW_WORKLOADS + ("softmax_4096x8192_bf16", "softmax_256x262144_bf16", "softmax_262144x128_bf16"):
         entry = {}
         impls = ("ours", "ours_noweight", "ref") if name == "rmsnorm_16384x4096" else ("ours", "ref")
         for impl in impls:
@@ -806,6 +817,9 @@ def sweep(args, world):
                 entry[impl]["check"] = bool(case.check())
             del case
             torch.cuda.empty_cache()
+        if name.endswith("_bf16"):  # the fp32 entry carries the end-to-end and CPU numbers of the shape
+            out[name] = entry
+            continue
         if name == "topk_512x151936":
             # data-dependent paths of the streaming top-k, timed beside the reference's kernel on the same rows
             adv = {}

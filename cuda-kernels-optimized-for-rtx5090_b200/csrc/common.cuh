@@ -200,6 +200,16 @@ __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.
 // Status word a kernel sets when a bounded wait gave up (0 = fine). One per library, read by <op>_status().
 #define CKB_STATUS_TIMEOUT 1u
 
+// ---------------------------------------------------------------------------------------------------------------
+// Programmatic dependent launch. A kernel launched with the programmatic-serialisation attribute may be scheduled
+// while the previous kernel on its stream is still finishing; pdl_wait() then blocks until that kernel has completed
+// and its memory operations are visible (so every read of an input and every write of an output comes after it),
+// and pdl_trigger() lets the next such kernel be scheduled once every CTA of this one has started. Both are no-ops
+// for a kernel launched without the attribute.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace ckb
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -225,6 +235,27 @@ inline int device_sm_count() {
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Launches kernel<<<grid, block, smem, stream>>>(args...) with programmatic stream serialisation allowed, so it can
+// overlap the tail of the kernel before it on the stream (its pdl_wait() keeps every data dependency).
+#ifndef CKB_PDL
+#define CKB_PDL 1  // 0: launch without programmatic serialisation (measurements)
+#endif
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = CKB_PDL ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 }  // namespace ckb
 
 #define CKB_EXPORT extern "C" __attribute__((visibility("default")))

@@ -77,6 +77,8 @@ template <typename T, typename WT, int VPT>
 __global__ void __launch_bounds__(256) rms_warp_rows(const T* __restrict__ x, const WT* __restrict__ w,
                                                      T* __restrict__ y, long long rows, int cols, float eps) {
   constexpr bool kW = !std::is_same<WT, NoWeight>::value;
+  pdl_wait();
+  pdl_trigger();
   const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;  // whole warps leave together: no shuffle is left waiting
   const int lane = threadIdx.x & 31;
@@ -123,6 +125,8 @@ __global__ void __launch_bounds__(VPT >= 8 ? 512 : 1024) rms_block_rows(const T*
                                                        T* __restrict__ y, int cols, float eps) {
   constexpr bool kW = !std::is_same<WT, NoWeight>::value;
   __shared__ float slots[32];
+  pdl_wait();
+  pdl_trigger();
   const int nvec = cols >> 3;
   const long long off = (long long)blockIdx.x * cols;
   const T* xr = x + off;
@@ -172,6 +176,8 @@ __global__ void __launch_bounds__(VPT >= 8 ? 512 : 1024) rms_block_rows(const T*
 template <typename T, typename WT>
 __global__ void __launch_bounds__(1024) rms_generic(const T* __restrict__ x, const WT* __restrict__ w,
                                                     T* __restrict__ y, int cols, float eps) {
+  pdl_wait();
+  pdl_trigger();
   constexpr bool kW = !std::is_same<WT, NoWeight>::value;
   __shared__ float slots[32];
   const long long off = (long long)blockIdx.x * cols;
@@ -208,13 +214,15 @@ constexpr int kBlockRowsMaxVec = 4096;    // block path: at most 512 threads x 8
 template <typename T, typename WT, int VPT>
 void start_warp(const void* x, const void* w, void* y, long long rows, int cols, float eps, cudaStream_t s) {
   const unsigned grid = (unsigned)((rows + 7) / 8);
-  rms_warp_rows<T, WT, VPT><<<grid, 256, 0, s>>>((const T*)x, (const WT*)w, (T*)y, rows, cols, eps);
+  launch_pdl(rms_warp_rows<T, WT, VPT>, dim3(grid), dim3(256), 0, s, (const T*)x, (const WT*)w, (T*)y, rows, cols,
+             eps);
 }
 
 template <typename T, typename WT, int VPT>
 void start_block(const void* x, const void* w, void* y, long long rows, int cols, int threads, float eps,
                  cudaStream_t s) {
-  rms_block_rows<T, WT, VPT><<<(unsigned)rows, threads, 0, s>>>((const T*)x, (const WT*)w, (T*)y, cols, eps);
+  launch_pdl(rms_block_rows<T, WT, VPT>, dim3((unsigned)rows), dim3(threads), 0, s, (const T*)x, (const WT*)w,
+             (T*)y, cols, eps);
 }
 
 template <typename T, typename WT>
@@ -242,7 +250,8 @@ int dispatch(const void* x, const void* w, void* y, long long rows, int cols, fl
     }
     return (int)cudaGetLastError();
   }
-  rms_generic<T, WT><<<(unsigned)rows, generic_threads, 0, s>>>((const T*)x, (const WT*)w, (T*)y, cols, eps);
+  launch_pdl(rms_generic<T, WT>, dim3((unsigned)rows), dim3(generic_threads), 0, s, (const T*)x, (const WT*)w, (T*)y,
+             cols, eps);
   return (int)cudaGetLastError();
 }
 

@@ -58,6 +58,8 @@ __global__ void __launch_bounds__(256, CKB_ROPE_MIN_BLOCKS) rope_tokens(const T*
                                                 const C* __restrict__ sin_rows, const float* __restrict__ inv_freq,
                                                 const long long* __restrict__ ids, T* q_out, T* k_out,
                                                 long long tokens, int q_heads, int kv_heads, int head_dim) {
+  pdl_wait();
+  pdl_trigger();
   const long long token = (long long)blockIdx.x * blockDim.z + threadIdx.z;
   if (token >= tokens) return;
   const int half = head_dim >> 1;
@@ -142,6 +144,8 @@ __global__ void __launch_bounds__(1024) rope_scalar(const T* q, const T* k, cons
                                                     const float* __restrict__ inv_freq,
                                                     const long long* __restrict__ ids, T* q_out, T* k_out,
                                                     int q_heads, int kv_heads, int head_dim) {
+  pdl_wait();
+  pdl_trigger();
   const long long token = blockIdx.x;
   const int half = head_dim >> 1;
   const long long pos = ids[token];
@@ -195,20 +199,20 @@ int start(const Args& a, cudaStream_t s) {
     if (grid > INT_MAX) return -1;
     const dim3 block(lanes, r, z);
     if (in_place) {
-      rope_tokens<T, C, kCache, true><<<(unsigned)grid, block, 0, s>>>(
-          (const T*)a.q, (const T*)a.k, (const C*)a.cos_rows, (const C*)a.sin_rows, a.inv_freq, a.ids, (T*)a.q_out,
-          (T*)a.k_out, a.tokens, a.q_heads, a.kv_heads, a.head_dim);
+      launch_pdl(rope_tokens<T, C, kCache, true>, dim3((unsigned)grid), block, 0, s, (const T*)a.q, (const T*)a.k,
+                 (const C*)a.cos_rows, (const C*)a.sin_rows, a.inv_freq, a.ids, (T*)a.q_out, (T*)a.k_out, a.tokens,
+                 a.q_heads, a.kv_heads, a.head_dim);
     } else {
-      rope_tokens<T, C, kCache, false><<<(unsigned)grid, block, 0, s>>>(
-          (const T*)a.q, (const T*)a.k, (const C*)a.cos_rows, (const C*)a.sin_rows, a.inv_freq, a.ids, (T*)a.q_out,
-          (T*)a.k_out, a.tokens, a.q_heads, a.kv_heads, a.head_dim);
+      launch_pdl(rope_tokens<T, C, kCache, false>, dim3((unsigned)grid), block, 0, s, (const T*)a.q, (const T*)a.k,
+                 (const C*)a.cos_rows, (const C*)a.sin_rows, a.inv_freq, a.ids, (T*)a.q_out, (T*)a.k_out, a.tokens,
+                 a.q_heads, a.kv_heads, a.head_dim);
     }
   } else {
     if (a.tokens > INT_MAX) return -1;
     const dim3 block(64, heads < 16 ? heads : 16);
-    rope_scalar<T, C, kCache><<<(unsigned)a.tokens, block, 0, s>>>(
-        (const T*)a.q, (const T*)a.k, (const C*)a.cos_rows, (const C*)a.sin_rows, a.inv_freq, a.ids, (T*)a.q_out,
-        (T*)a.k_out, a.q_heads, a.kv_heads, a.head_dim);
+    launch_pdl(rope_scalar<T, C, kCache>, dim3((unsigned)a.tokens), block, 0, s, (const T*)a.q, (const T*)a.k,
+               (const C*)a.cos_rows, (const C*)a.sin_rows, a.inv_freq, a.ids, (T*)a.q_out, (T*)a.k_out, a.q_heads,
+               a.kv_heads, a.head_dim);
   }
   return (int)cudaGetLastError();
 }
@@ -237,6 +241,8 @@ __global__ void __launch_bounds__(256) rope_kv_tokens(const T* q, const T* k, co
                                                       const long long* __restrict__ slots, T* q_out, T* k_out,
                                                       T* __restrict__ key_cache, T* __restrict__ value_cache,
                                                       long long tokens, int q_heads, int kv_heads, int head_dim) {
+  pdl_wait();
+  pdl_trigger();
   const long long token = (long long)blockIdx.x * blockDim.z + threadIdx.z;
   if (token >= tokens) return;
   const int half = head_dim >> 1;
@@ -321,6 +327,8 @@ __global__ void __launch_bounds__(1024) rope_kv_scalar(const T* q, const T* k, c
                                                        const long long* __restrict__ slots, T* q_out, T* k_out,
                                                        T* __restrict__ key_cache, T* __restrict__ value_cache,
                                                        int q_heads, int kv_heads, int head_dim) {
+  pdl_wait();
+  pdl_trigger();
   const long long token = blockIdx.x;
   const int half = head_dim >> 1;
   const long long pos = ids[token], slot = slots[token];
@@ -386,21 +394,19 @@ int start_kv(const KvArgs& a, cudaStream_t s) {
     if (grid > INT_MAX) return -1;
     const dim3 block(lanes, r, z);
     if (in_place)
-      rope_kv_tokens<T, C, true><<<(unsigned)grid, block, 0, s>>>(
-          (const T*)a.q, (const T*)a.k, (const T*)a.v, (const C*)a.cos_rows, (const C*)a.sin_rows, a.ids, a.slots,
-          (T*)a.q_out, (T*)a.k_out, (T*)a.key_cache, (T*)a.value_cache, a.tokens, a.q_heads, a.kv_heads,
-          a.head_dim);
+      launch_pdl(rope_kv_tokens<T, C, true>, dim3((unsigned)grid), block, 0, s, (const T*)a.q, (const T*)a.k,
+                 (const T*)a.v, (const C*)a.cos_rows, (const C*)a.sin_rows, a.ids, a.slots, (T*)a.q_out,
+                 (T*)a.k_out, (T*)a.key_cache, (T*)a.value_cache, a.tokens, a.q_heads, a.kv_heads, a.head_dim);
     else
-      rope_kv_tokens<T, C, false><<<(unsigned)grid, block, 0, s>>>(
-          (const T*)a.q, (const T*)a.k, (const T*)a.v, (const C*)a.cos_rows, (const C*)a.sin_rows, a.ids, a.slots,
-          (T*)a.q_out, (T*)a.k_out, (T*)a.key_cache, (T*)a.value_cache, a.tokens, a.q_heads, a.kv_heads,
-          a.head_dim);
+      launch_pdl(rope_kv_tokens<T, C, false>, dim3((unsigned)grid), block, 0, s, (const T*)a.q, (const T*)a.k,
+                 (const T*)a.v, (const C*)a.cos_rows, (const C*)a.sin_rows, a.ids, a.slots, (T*)a.q_out,
+                 (T*)a.k_out, (T*)a.key_cache, (T*)a.value_cache, a.tokens, a.q_heads, a.kv_heads, a.head_dim);
   } else {
     if (a.tokens > INT_MAX) return -1;
     const dim3 block(64, heads < 16 ? heads : 16);
-    rope_kv_scalar<T, C><<<(unsigned)a.tokens, block, 0, s>>>(
-        (const T*)a.q, (const T*)a.k, (const T*)a.v, (const C*)a.cos_rows, (const C*)a.sin_rows, a.ids, a.slots,
-        (T*)a.q_out, (T*)a.k_out, (T*)a.key_cache, (T*)a.value_cache, a.q_heads, a.kv_heads, a.head_dim);
+    launch_pdl(rope_kv_scalar<T, C>, dim3((unsigned)a.tokens), block, 0, s, (const T*)a.q, (const T*)a.k,
+               (const T*)a.v, (const C*)a.cos_rows, (const C*)a.sin_rows, a.ids, a.slots, (T*)a.q_out, (T*)a.k_out,
+               (T*)a.key_cache, (T*)a.value_cache, a.q_heads, a.kv_heads, a.head_dim);
   }
   return (int)cudaGetLastError();
 }

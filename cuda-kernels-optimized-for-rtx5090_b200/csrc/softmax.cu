@@ -151,6 +151,8 @@ __device__ __forceinline__ float exp_vec2(float (&f)[V], const ExpShift& es) {
 // G lanes per row (4..32), NV vectors per lane, 256 threads = 8 warps = 8 * 32 / G rows per block.
 template <typename T, int G, int NV>
 __global__ void __launch_bounds__(256) sm_group(const T* __restrict__ x, T* __restrict__ y, long long rows, int cols) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int V = VecN<T>::N;
   constexpr int RPW = 32 / G;
   const int lane = threadIdx.x & 31;
@@ -197,6 +199,8 @@ __global__ void __launch_bounds__(256) sm_group(const T* __restrict__ x, T* __re
 // One block per row; thread t keeps vectors t, t + B, ..., t + B (NV - 1).
 template <typename T, int NV, int MAXT>
 __global__ void __launch_bounds__(MAXT) sm_block(const T* __restrict__ x, T* __restrict__ y, int cols) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int V = VecN<T>::N;
   __shared__ float red_m[32];
   __shared__ double red_s[32];
@@ -341,6 +345,8 @@ template <typename T>
 __global__ void __launch_bounds__(kClusterThreads, 3) sm_cluster(const T* __restrict__ x, T* __restrict__ y,
                                                               long long rows, long long cols, int slice,
                                                               int stages, int stage_vec) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int V = VecN<T>::N;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t bars[kMaxStages];
@@ -515,6 +521,8 @@ __device__ __forceinline__ uint4 neg_inf16(const __nv_bfloat16*) {
 template <typename T, int U>
 __global__ void __launch_bounds__(kStreamThreads, 2) sm_cluster_stream(const T* __restrict__ x, T* __restrict__ y,
                                                                       long long rows, long long cols, long long sv) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int V = VecN<T>::N;
   constexpr int kWarps = kStreamThreads / 32;
   constexpr long long kStep = (long long)kStreamThreads * U;
@@ -657,6 +665,8 @@ __global__ void __launch_bounds__(kStreamThreads, 2) sm_cluster_stream(const T* 
 // and third reads of a row mostly hit L2.
 template <typename T>
 __global__ void __launch_bounds__(1024) sm_stream(const T* __restrict__ x, T* __restrict__ y, long long cols) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[32];
   __shared__ double red_d[32];
   const T* xr = x + (long long)blockIdx.x * cols;
@@ -677,7 +687,7 @@ int start_group(const T* x, T* y, long long rows, int cols, cudaStream_t s) {
   constexpr long long rows_per_block = 8 * (32 / G);
   const long long grid = (rows + rows_per_block - 1) / rows_per_block;
   if (grid > INT_MAX) return -1;
-  sm_group<T, G, NV><<<(unsigned)grid, 256, 0, s>>>(x, y, rows, cols);
+  launch_pdl(sm_group<T, G, NV>, dim3((unsigned)grid), dim3(256), 0, s, x, y, rows, cols);
   return (int)cudaGetLastError();
 }
 
@@ -685,8 +695,8 @@ int start_group(const T* x, T* y, long long rows, int cols, cudaStream_t s) {
 template <typename T, int NV>
 int start_block(const T* x, T* y, long long rows, int cols, int threads, cudaStream_t s) {
   if (rows > INT_MAX) return -1;
-  if (threads <= 512) sm_block<T, NV, 512><<<(unsigned)rows, threads, 0, s>>>(x, y, cols);
-  else sm_block<T, NV, 1024><<<(unsigned)rows, threads, 0, s>>>(x, y, cols);
+  if (threads <= 512) launch_pdl(sm_block<T, NV, 512>, dim3((unsigned)rows), dim3(threads), 0, s, x, y, cols);
+  else launch_pdl(sm_block<T, NV, 1024>, dim3((unsigned)rows), dim3(threads), 0, s, x, y, cols);
   return (int)cudaGetLastError();
 }
 
@@ -711,12 +721,14 @@ cudaLaunchConfig_t cluster_config(int cl, unsigned grid_y, int smem, cudaStream_
   attr[0].val.clusterDim.x = (unsigned)cl;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see launch_pdl
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.gridDim = dim3((unsigned)cl, grid_y, 1);
   cfg.blockDim = dim3(kClusterThreads, 1, 1);
   cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = CKB_PDL ? 2 : 1;
   return cfg;
 }
 
@@ -755,8 +767,9 @@ ClusterPlan plan_cluster(long long cols, bool ring) {
       cudaGetLastError();
       continue;
     }
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg = cluster_config(cl, 1, smem, nullptr, attr);
+    cfg.numAttrs = 1;  // the cluster shape alone for the occupancy query
     int active = 0;
     if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess) {
       cudaGetLastError();
@@ -796,7 +809,7 @@ int start_cluster(const ClusterPlan& p, const T* x, T* y, long long rows, long l
   // grid's y limit: then as many clusters as stay resident loop over the rows with a ring of slice buffers.
   const long long g = p.ring ? (rows < p.active ? rows : p.active) : rows;
   if (g > 65535) return -2;  // grid.y limit: the caller falls back
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = cluster_config(p.cl, (unsigned)g, smem, s, attr);
   const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, x, y, rows, cols, p.slice, p.stages, p.stage_vec);
   if (err != cudaSuccess) return (int)err;
@@ -819,15 +832,18 @@ int start_cluster_stream(const T* x, T* y, long long rows, long long cols, cudaS
   }
   const long long sv = (nvec + cl - 1) / cl;
   const unsigned gy = (unsigned)(rows < 65535 ? rows : 65535);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = cluster_config(cl, 1, 0, s, attr);
   cfg.blockDim = dim3(kStreamThreads, 1, 1);
+  const unsigned launch_attrs = cfg.numAttrs;
+  cfg.numAttrs = 1;  // the cluster shape alone for the occupancy query
   int active = 0;
   if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess || active <= 0) {
     cudaGetLastError();
     return -2;
   }
   cfg.gridDim = dim3((unsigned)cl, gy, 1);
+  cfg.numAttrs = launch_attrs;
   const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, x, y, rows, cols, sv);
   if (err != cudaSuccess) return (int)err;
   return (int)cudaGetLastError();
@@ -877,7 +893,7 @@ int dispatch(const T* x, T* y, long long rows, long long cols, cudaStream_t s) {
     }
   }
   if (rows > INT_MAX) return -1;
-  sm_stream<T><<<(unsigned)rows, 1024, 0, s>>>(x, y, cols);
+  launch_pdl(sm_stream<T>, dim3((unsigned)rows), dim3(1024), 0, s, x, y, cols);
   return (int)cudaGetLastError();
 }
 

@@ -804,6 +804,8 @@ __device__ void finish_segment(const SegArgs& a, long long row, int seg, int nse
 // the body's first aligned address go with segment 0, those after its end with the last segment.
 template <typename T, int NT>
 __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const SegArgs a) {
+  pdl_wait();
+  pdl_trigger();
   using C = Cfg<NT, sizeof(T)>;
   constexpr int V = VecN<T>::N;
   constexpr int kThreads = NT, kWarps = C::kWarps, kU = C::kU, kStages = C::kStages, kTileVecs = C::kTileVecs;
@@ -1111,6 +1113,8 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
 template <typename T>
 __global__ void __launch_bounds__(256) topk_merge(const u64* __restrict__ lists, int nlists, long long rows, int k,
                                                   T* __restrict__ values, long long* __restrict__ indices) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) u64 sl[];
   const long long row = blockIdx.x;
   const int total = nlists * k;
@@ -1141,6 +1145,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) topk_merge_wait(const u64* lists, const unsigned* flags, int world,
                                                        unsigned epoch, long long rows, int k, T* __restrict__ values,
                                                        long long* __restrict__ indices) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) u64 sl[];
   __shared__ int s_timeout;
   const long long row = blockIdx.x;
@@ -1228,7 +1234,8 @@ int start_shape(const SegArgs& a, long long rows, long long nseg, cudaStream_t s
     cudaGetLastError();
     return (int)e;
   }
-  topk_stream<T, NT><<<dim3((unsigned)nseg, (unsigned)rows), NT, Cfg<NT, sizeof(T)>::kSmemBytes, s>>>(a);
+  launch_pdl(topk_stream<T, NT>, dim3((unsigned)nseg, (unsigned)rows), dim3(NT), Cfg<NT, sizeof(T)>::kSmemBytes, s,
+             a);
   return (int)cudaGetLastError();
 }
 
@@ -1356,14 +1363,14 @@ CKB_EXPORT int ckb_topk_merge_launch(const unsigned long long* lists, int nlists
     if (cudaFuncSetAttribute(topk_merge<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
       return (int)cudaGetLastError();
-    topk_merge<float><<<(unsigned)rows, 256, (size_t)smem, stream>>>((const u64*)lists, nlists, rows, k,
-                                                                     (float*)values, (long long*)indices);
+    launch_pdl(topk_merge<float>, dim3((unsigned)rows), dim3(256), (size_t)smem, stream, (const u64*)lists, nlists,
+               rows, k, (float*)values, (long long*)indices);
   } else if (dtype == kBF16) {
     if (cudaFuncSetAttribute(topk_merge<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
         cudaSuccess)
       return (int)cudaGetLastError();
-    topk_merge<__nv_bfloat16><<<(unsigned)rows, 256, (size_t)smem, stream>>>(
-        (const u64*)lists, nlists, rows, k, (__nv_bfloat16*)values, (long long*)indices);
+    launch_pdl(topk_merge<__nv_bfloat16>, dim3((unsigned)rows), dim3(256), (size_t)smem, stream, (const u64*)lists,
+               nlists, rows, k, (__nv_bfloat16*)values, (long long*)indices);
   } else {
     return -1;
   }
@@ -1423,15 +1430,14 @@ CKB_EXPORT int ckb_topk_merge_wait_launch(const unsigned long long* lists, const
     if (cudaFuncSetAttribute(topk_merge_wait<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return (int)cudaGetLastError();
-    topk_merge_wait<float><<<(unsigned)rows, 256, (size_t)smem, stream>>>((const u64*)lists, flags, world, epoch,
-                                                                          rows, k, (float*)values,
-                                                                          (long long*)indices);
+    launch_pdl(topk_merge_wait<float>, dim3((unsigned)rows), dim3(256), (size_t)smem, stream, (const u64*)lists,
+               flags, world, epoch, rows, k, (float*)values, (long long*)indices);
   } else if (dtype == kBF16) {
     if (cudaFuncSetAttribute(topk_merge_wait<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return (int)cudaGetLastError();
-    topk_merge_wait<__nv_bfloat16><<<(unsigned)rows, 256, (size_t)smem, stream>>>(
-        (const u64*)lists, flags, world, epoch, rows, k, (__nv_bfloat16*)values, (long long*)indices);
+    launch_pdl(topk_merge_wait<__nv_bfloat16>, dim3((unsigned)rows), dim3(256), (size_t)smem, stream,
+               (const u64*)lists, flags, world, epoch, rows, k, (__nv_bfloat16*)values, (long long*)indices);
   } else {
     return -1;
   }
