@@ -119,9 +119,16 @@ __global__ void __launch_bounds__(256) rms_warp_rows(const T* __restrict__ x, co
   }
 }
 
+// Block-size bound of rms_block_rows: fp32 weights hold twice the registers per vector, so their shapes stop at
+// half the threads (the dispatcher sends longer fp32-weighted rows to rms_generic).
+template <typename WT, int VPT>
+constexpr int block_rows_bound() {
+  return std::is_same<WT, float>::value ? (VPT >= 8 ? 256 : 512) : (VPT >= 8 ? 512 : 1024);
+}
+
 // One block per row, thread t holding vectors t, t + B, ..., t + B (VPT - 1) (B = blockDim.x).
 template <typename T, typename WT, int VPT>
-__global__ void __launch_bounds__(VPT >= 8 ? 512 : 1024) rms_block_rows(const T* __restrict__ x, const WT* __restrict__ w,
+__global__ void __launch_bounds__(block_rows_bound<WT, VPT>()) rms_block_rows(const T* __restrict__ x, const WT* __restrict__ w,
                                                        T* __restrict__ y, int cols, float eps) {
   constexpr bool kW = !std::is_same<WT, NoWeight>::value;
   __shared__ float slots[32];
@@ -236,7 +243,7 @@ int dispatch(const void* x, const void* w, void* y, long long rows, int cols, fl
     else start_warp<T, WT, 4>(x, w, y, rows, cols, eps, s);
     return (int)cudaGetLastError();
   }
-  if (vec && nvec <= kBlockRowsMaxVec) {
+  if (vec && nvec <= (std::is_same<WT, float>::value ? kBlockRowsMaxVec / 2 : kBlockRowsMaxVec)) {
     constexpr int target = std::is_same<WT, NoWeight>::value ? CKB_RMSNORM_TARGET_THREADS
                                                              : CKB_RMSNORM_TARGET_THREADS_W;
     int vpt = 1;
