@@ -341,8 +341,11 @@ __device__ __forceinline__ void cluster_store(const uint4* buf, uint4* dst, int 
 // -> every thread scales and stores. One exchange per row, and no thread waits for the row max before its
 // exponentials. The exchange slots and their mbarrier are double buffered by row parity, so a fast CTA's next row
 // never lands in a slot a slow peer still reads.
+#ifndef CKB_SOFTMAX_CLUSTER_MINB_16
+#define CKB_SOFTMAX_CLUSTER_MINB_16 3  // resident CTAs per SM the 16-bit instantiation is compiled for
+#endif
 template <typename T>
-__global__ void __launch_bounds__(kClusterThreads, 3) sm_cluster(const T* __restrict__ x, T* __restrict__ y,
+__global__ void __launch_bounds__(kClusterThreads, sizeof(T) == 2 ? CKB_SOFTMAX_CLUSTER_MINB_16 : 3) sm_cluster(const T* __restrict__ x, T* __restrict__ y,
                                                               long long rows, long long cols, int slice,
                                                               int stages, int stage_vec) {
   pdl_wait();
