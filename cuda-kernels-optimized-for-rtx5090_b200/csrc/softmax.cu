@@ -248,7 +248,9 @@ __global__ void __launch_bounds__(MAXT) sm_block(const T* __restrict__ x, T* __r
 }
 
 // ---------------------------------------------------------------------------------------------- cluster path ----
-constexpr int kClusterThreads = 384;
+constexpr int kClusterThreads = 256;
+constexpr int kClusterMinBlocks = 4;  // registers for four CTAs per SM (64 per thread)
+constexpr int kTailVecs = 4;          // tail vectors per thread: a slice may keep 16 KB out of shared memory
 constexpr int kMaxStages = 4;
 
 // The start-up handshake: the initialising thread's fence.mbarrier_init (release, cluster scope) already publishes the
@@ -298,15 +300,15 @@ __device__ __forceinline__ void st_async_u64(unsigned raddr, unsigned long long 
 
 constexpr int kMaxCluster = 16;
 
-// Pass 3 of the cluster path: y = E * s1 (* s2) for the slice held in shared memory (fp32: the exponentials in
-// place; bf16: the raw values, whose exponentials are taken again), streamed to HBM.
+// Pass 3 of the cluster path: y = E * s1 (* s2) for the staged part of the slice (fp32: the exponentials in place;
+// bf16: the raw values, whose exponentials are taken again), streamed to HBM.
 template <typename T, bool kTwo>
-__device__ __forceinline__ void cluster_store(const uint4* buf, uint4* dst, int nv, float s1, float s2,
+__device__ __forceinline__ void cluster_store(const uint4* buf, uint4* dst, int ns, float s1, float s2,
                                               const ExpShift& es) {
   constexpr int V = VecN<T>::N;
   const float2 m1 = make_float2(s1, s1), m2 = make_float2(s2, s2);
 #pragma unroll 4
-  for (int i = threadIdx.x; i < nv; i += kClusterThreads) {
+  for (int i = threadIdx.x; i < ns; i += kClusterThreads) {
     const uint4 raw = buf[i];
     if constexpr (V == 4) {
       float2 a = __fmul2_rn(make_float2(__uint_as_float(raw.x), __uint_as_float(raw.y)), m1);
@@ -332,22 +334,40 @@ __device__ __forceinline__ void cluster_store(const uint4* buf, uint4* dst, int 
   }
 }
 
-// Grid (CL, G), cluster (CL, 1, 1): cluster g handles rows g, g + G, g + 2G, ... and CTA `rank` owns elements
-// [rank * slice, min((rank + 1) * slice, cols)) of each (slice and cols multiples of the 16-byte vector). A CTA cycles
-// its rows through `stages` slice buffers in dynamic shared memory (stride `stage_vec` 16-byte vectors): the bulk copy
-// of a row is issued `stages` rows ahead. Per row: the slice's max m_c -> exp(x - m_c) in place (fp32) and their sum
-// s_c -> warp 0 st.asyncs (m_c, s_c) to every peer -> warp 0 combines the cluster's pairs in fp64 into the row max M,
-// the row sum S = sum of s_l * exp(m_l - M) and this slice's scale exp(m_c - M) / S, broadcast through shared memory
-// -> every thread scales and stores. One exchange per row, and no thread waits for the row max before its
-// exponentials. The exchange slots and their mbarrier are double buffered by row parity, so a fast CTA's next row
-// never lands in a slot a slow peer still reads.
-#ifndef CKB_SOFTMAX_CLUSTER_MINB_16
-#define CKB_SOFTMAX_CLUSTER_MINB_16 3  // resident CTAs per SM the 16-bit instantiation is compiled for
-#endif
+// The slice's tail, vectors [ns, nv) held in registers: thread t owns vectors ns + t + j * kClusterThreads.
+__device__ __forceinline__ uint4 neg_inf16(const float*) {
+  return make_uint4(0xff800000u, 0xff800000u, 0xff800000u, 0xff800000u);
+}
+__device__ __forceinline__ uint4 neg_inf16(const __nv_bfloat16*) {
+  return make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
+}
 template <typename T>
-__global__ void __launch_bounds__(kClusterThreads, sizeof(T) == 2 ? CKB_SOFTMAX_CLUSTER_MINB_16 : 3) sm_cluster(const T* __restrict__ x, T* __restrict__ y,
-                                                              long long rows, long long cols, int slice,
-                                                              int stages, int stage_vec) {
+__device__ __forceinline__ void tail_load(uint4 (&tv)[kTailVecs], const uint4* src, int ns, int nv) {
+#pragma unroll
+  for (int j = 0; j < kTailVecs; ++j) {
+    const int i = ns + (int)threadIdx.x + j * kClusterThreads;
+    tv[j] = i < nv ? __ldcg(src + i) : neg_inf16((const T*)nullptr);
+  }
+}
+
+// Grid (CL, G), cluster (CL, 1, 1): cluster g handles rows g, g + G, g + 2G, ... and CTA `rank` owns elements
+// [rank * slice, min((rank + 1) * slice, cols)) of each (slice and cols multiples of the 16-byte vector). Of its nv
+// vectors, the first ns = min(nv, ns_cap) are staged in shared memory by one bulk copy and the rest (at most
+// kClusterThreads * kTailVecs, the tail) are read into registers beside it: a 64 KB slice fits four CTAs per SM that
+// way, where staging all of it fits three. A CTA cycles its rows through `stages` slice buffers in dynamic shared
+// memory (stride `stage_vec` 16-byte vectors): the bulk copy of a row is issued `stages` rows ahead. Per row: the
+// slice's max m_c -> exp(x - m_c) (in place for the staged fp32 part) and their sum s_c -> warp 0 st.asyncs (m_c, s_c)
+// to every peer -> warp 0 combines the cluster's pairs in fp64 into the row max M, the row sum S = sum of
+// s_l * exp(m_l - M) and this slice's scale exp(m_c - M) / S, broadcast through shared memory -> every thread scales
+// and stores. One exchange per row, and no thread waits for the row max before its exponentials. The exchange slots
+// and their mbarrier are double buffered by row parity, so a fast CTA's next row never lands in a slot a slow peer
+// still reads.
+// kRing false: one row per cluster (grid y = rows), one buffer, no refills.
+template <typename T, bool kRing>
+__global__ void __launch_bounds__(kClusterThreads, kClusterMinBlocks) sm_cluster(const T* __restrict__ x,
+                                                                             T* __restrict__ y, long long rows,
+                                                                             long long cols, int slice, int ns_cap,
+                                                                             int stages_arg, int stage_vec) {
   pdl_wait();
   pdl_trigger();
   constexpr int V = VecN<T>::N;
@@ -366,10 +386,12 @@ __global__ void __launch_bounds__(kClusterThreads, sizeof(T) == 2 ? CKB_SOFTMAX_
   const long long beg = (long long)rank * slice;
   long long n = cols - beg;
   n = n < 0 ? 0 : (n > slice ? slice : n);
-  const int nv = (int)(n / V);  // vectors of this CTA's slice (the same for every row)
-  const unsigned bytes = (unsigned)nv * 16u;
+  const int nv = (int)(n / V);                 // vectors of this CTA's slice (the same for every row)
+  const int ns = nv < ns_cap ? nv : ns_cap;    // of which staged in shared memory; [ns, nv) is the tail
+  const unsigned bytes = (unsigned)ns * 16u;
   uint4* const buf0 = reinterpret_cast<uint4*>(smem_raw);
   const long long first = blockIdx.y, step = gridDim.y;
+  const int stages = kRing ? stages_arg : 1;
 
   if (threadIdx.x == 0) {
     for (int st = 0; st < stages; ++st) mbar_init(&bars[st], 1);
@@ -385,6 +407,12 @@ __global__ void __launch_bounds__(kClusterThreads, sizeof(T) == 2 ? CKB_SOFTMAX_
         }
       }
   }
+  // The first row's tail goes out beside its bulk copy; each later row's is loaded at the end of the row before.
+  uint4 tv[kTailVecs];
+  if (first < rows) tail_load<T>(tv, reinterpret_cast<const uint4*>(x + first * cols + beg), ns, nv);
+  // No thread polls a copy mbarrier before thread 0 has initialised it (shared memory still holds whatever the SM's
+  // previous CTA left at these addresses, possibly a completed mbarrier of the same layout).
+  __syncthreads();
   // Every CTA's exchange mbarriers are initialised before any peer sends to them: every thread arrives here, and
   // warp 0, the only one that touches peers, waits for the whole cluster before its first send.
   cluster_arrive();
@@ -404,16 +432,24 @@ __global__ void __launch_bounds__(kClusterThreads, sizeof(T) == 2 ? CKB_SOFTMAX_
   bool ok = true;
   int t = 0;
   for (long long row = first; row < rows; row += step, ++t) {
-    const int st = t % stages;
-    const int p = t & 1;
+    const int st = kRing ? t % stages : 0;
+    const int p = kRing ? t & 1 : 0;
     uint4* const buf = buf0 + (size_t)st * stage_vec;
     if (threadIdx.x == 0) mbar_arrive_expect_tx(&bar_pair[p], csize * 12u);
-    if (bytes) ok = mbar_wait(&bars[st], (unsigned)(t / stages) & 1u) && ok;
 
-    // Pass 1: the slice's max m_c (NaN-propagating), folded by every warp from the per-warp maxima.
+    // Pass 1: the slice's max m_c (NaN-propagating), folded by every warp from the per-warp maxima; the tail (whose
+    // loads usually land first) before the wait for the staged part.
     float m = -CUDART_INF_F;
+#pragma unroll
+    for (int j = 0; j < kTailVecs; ++j) {
+      float f[V];
+      unpack16(tv[j], f, x);
+#pragma unroll
+      for (int q = 0; q < V; ++q) m = max_nan(m, f[q]);
+    }
+    if (bytes) ok = mbar_wait(&bars[st], (unsigned)(t / stages) & 1u) && ok;
 #pragma unroll 4
-    for (int i = threadIdx.x; i < nv; i += kClusterThreads) {
+    for (int i = threadIdx.x; i < ns; i += kClusterThreads) {
       float f[V];
       unpack16(buf[i], f, x);
 #pragma unroll
@@ -426,10 +462,11 @@ __global__ void __launch_bounds__(kClusterThreads, sizeof(T) == 2 ? CKB_SOFTMAX_
     // A slice of -inf only takes its (zero) exponentials against 0; its pair still reports m_c = -inf.
     const ExpShift es(mc == -CUDART_INF_F ? 0.0f : mc);
 
-    // Pass 2: exp(x - m_c), summed pairwise per vector into fp64; fp32 slices keep the exponentials in place.
+    // Pass 2: exp(x - m_c), summed pairwise per vector into fp64; the staged fp32 part keeps its exponentials in
+    // place, the tail keeps its raw values (its exponentials are taken again in pass 3).
     double sum = 0.0;
 #pragma unroll 4
-    for (int i = threadIdx.x; i < nv; i += kClusterThreads) {
+    for (int i = threadIdx.x; i < ns; i += kClusterThreads) {
       const uint4 raw = buf[i];
       if constexpr (V == 4) {
         const float2 a = exp_pair(make_float2(__uint_as_float(raw.x), __uint_as_float(raw.y)), es);
@@ -446,6 +483,20 @@ __global__ void __launch_bounds__(kClusterThreads, sizeof(T) == 2 ? CKB_SOFTMAX_
         const float2 s01 = __fadd2_rn(e[0], e[1]), s23 = __fadd2_rn(e[2], e[3]);
         const float2 s03 = __fadd2_rn(s01, s23);
         sum += (double)(s03.x + s03.y);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kTailVecs; ++j) {
+      if (ns + (int)threadIdx.x + j * kClusterThreads < nv) {
+        float f[V];
+        unpack16(tv[j], f, x);
+        float2 e[V / 2];
+#pragma unroll
+        for (int q = 0; q < V / 2; ++q) e[q] = exp2v<T>(make_float2(f[2 * q], f[2 * q + 1]), es);
+        float2 acc = __fadd2_rn(e[0], e[1]);
+#pragma unroll
+        for (int q = 2; q < V / 2; q += 2) acc = __fadd2_rn(acc, __fadd2_rn(e[q], e[q + 1]));
+        sum += (double)(acc.x + acc.y);
       }
     }
     sum = warp_sum(sum);
@@ -484,13 +535,32 @@ __global__ void __launch_bounds__(kClusterThreads, sizeof(T) == 2 ? CKB_SOFTMAX_
     }
     __syncthreads();
 
-    // Pass 3: scale from shared memory, stream to HBM (the two-factor form only when the factor needs it).
+    // Pass 3: scale from shared memory, stream to HBM (the two-factor form only when the factor needs it): the tail
+    // from its registers, then the staged part.
     uint4* const dst = reinterpret_cast<uint4*>(y + row * cols + beg);
-    if (scale_lo == 1.0f) cluster_store<T, false>(buf, dst, nv, scale, 1.0f, es);
-    else cluster_store<T, true>(buf, dst, nv, scale, scale_lo, es);
+    const float s1 = scale, s2 = scale_lo;
+#pragma unroll
+    for (int j = 0; j < kTailVecs; ++j) {
+      const int i = ns + (int)threadIdx.x + j * kClusterThreads;
+      if (i < nv) {
+        float f[V];
+        unpack16(tv[j], f, x);
+#pragma unroll
+        for (int q = 0; q < V / 2; ++q) {
+          float2 e = __fmul2_rn(exp2v<T>(make_float2(f[2 * q], f[2 * q + 1]), es), make_float2(s1, s1));
+          if (s2 != 1.0f) e = __fmul2_rn(e, make_float2(s2, s2));
+          f[2 * q] = e.x;
+          f[2 * q + 1] = e.y;
+        }
+        st_stream(dst + i, pack16(f, x));
+      }
+    }
+    if (s2 == 1.0f) cluster_store<T, false>(buf, dst, ns, s1, 1.0f, es);
+    else cluster_store<T, true>(buf, dst, ns, s1, s2, es);
     // Refill this buffer `stages` rows ahead once every thread is done with it (the exponentials written into it by
     // the generic proxy are ordered before the bulk copy's writes by the proxy fence). With no row left for the
     // buffer, the CTA just finishes. The barrier also keeps `scale` and `red` from being rewritten while read.
+    if (!kRing) break;
     const long long next = row + (long long)stages * step;
     if (next < rows) {
       if (bytes) fence_proxy_async();
@@ -500,6 +570,7 @@ __global__ void __launch_bounds__(kClusterThreads, sizeof(T) == 2 ? CKB_SOFTMAX_
         bulk_load(buf, x + next * cols + beg, bytes, &bars[st]);
       }
     }
+    if (row + step < rows) tail_load<T>(tv, reinterpret_cast<const uint4*>(x + (row + step) * cols + beg), ns, nv);
   }
   if (!ok) atomicOr(&g_softmax_status, CKB_STATUS_TIMEOUT);
 }
@@ -514,12 +585,6 @@ __global__ void __launch_bounds__(kClusterThreads, sizeof(T) == 2 ? CKB_SOFTMAX_
 constexpr int kStreamThreads = 512;
 constexpr int kStreamMaxCluster = 8;  // measured best for 4 MB rows (16-CTA clusters at 2 CTAs/SM pack worse)
 
-__device__ __forceinline__ uint4 neg_inf16(const float*) {
-  return make_uint4(0xff800000u, 0xff800000u, 0xff800000u, 0xff800000u);
-}
-__device__ __forceinline__ uint4 neg_inf16(const __nv_bfloat16*) {
-  return make_uint4(0xff80ff80u, 0xff80ff80u, 0xff80ff80u, 0xff80ff80u);
-}
 
 template <typename T, int U>
 __global__ void __launch_bounds__(kStreamThreads, 2) sm_cluster_stream(const T* __restrict__ x, T* __restrict__ y,
@@ -704,14 +769,19 @@ int start_block(const T* x, T* y, long long rows, int cols, int threads, cudaStr
 }
 
 constexpr long long kMaxRingBytes = 200 * 1024;
-#ifndef CKB_SOFTMAX_SLICE_TARGET
-#define CKB_SOFTMAX_SLICE_TARGET (64 * 1024)
+// Shared memory a slice stages before the rest goes to the register tail: 52 KB keeps four CTAs per SM (measured on
+// 64 KB slices: 48 KB staged + 16 KB tail 91.6 us, 52 + 12 89.6 us, 55 + 9 91.2 us, all 64 KB staged at three CTAs
+// per SM 104.6 us).
+#ifndef CKB_SOFTMAX_STAGE_TARGET
+#define CKB_SOFTMAX_STAGE_TARGET (52 * 1024)
 #endif
-constexpr long long kSliceTarget = CKB_SOFTMAX_SLICE_TARGET;
+constexpr long long kStageTargetVec = CKB_SOFTMAX_STAGE_TARGET / 16;
+constexpr long long kTailCapVec = (long long)kClusterThreads * kTailVecs;
 
 struct ClusterPlan {
   int cl = 0;         // 0: no cluster configuration fits
   int slice = 0;      // elements per CTA
+  int ns_cap = 0;     // vectors of a slice staged in shared memory (the rest, at most kTailCapVec, in registers)
   int stages = 0;     // slice buffers per CTA
   int stage_vec = 0;  // 16-byte vectors between buffers
   int active = 0;     // co-resident clusters
@@ -736,9 +806,12 @@ cudaLaunchConfig_t cluster_config(int cl, unsigned grid_y, int smem, cudaStream_
 }
 
 // The cluster shape for rows of `cols` elements. For each cluster size CL in 16, 8, 4, 2 the slice is cols / CL; a CTA
-// holds one slice buffer (or, for the persistent ring, as many as fit in 200 KB, at most 4) and
-// cudaOccupancyMaxActiveClusters says how many such clusters stay resident; the score is resident CTAs, doubled for
-// a ring of two or more buffers. Cached per (device, cols, ring); the cache holds the last shape asked for.
+// stages min(slice, 52 KB) of it in shared memory (more when the rest would exceed the register tail's 16 KB) in one
+// buffer (or, for the persistent ring, the whole slice in as many buffers as fit in 200 KB, at most 4), and
+// cudaOccupancyMaxActiveClusters says
+// how many such clusters stay resident. The score is resident CTAs, doubled for a ring of two or more buffers; a tie
+// goes to the smaller cluster (fewer CTAs exchange per row). Cached per (device, cols, ring); the cache holds the last
+// shape asked for.
 template <typename T>
 ClusterPlan plan_cluster(long long cols, bool ring) {
   constexpr int V = VecN<T>::N;
@@ -756,11 +829,14 @@ ClusterPlan plan_cluster(long long cols, bool ring) {
   ClusterPlan best;
   best.ring = ring;
   long long best_score = 0;
-  auto kern = sm_cluster<T>;
+  auto kern = ring ? sm_cluster<T, true> : sm_cluster<T, false>;
   for (int cl = 16; cl >= 2; cl /= 2) {
     const long long slice = ((cols + cl - 1) / cl + V - 1) / V * V;
-    const long long stage_bytes = (slice * (long long)sizeof(T) + 127) / 128 * 128;
-    long long stages = kMaxRingBytes / stage_bytes;
+    const long long slice_vec = slice / V;
+    long long ns_cap = slice_vec < kStageTargetVec ? slice_vec : kStageTargetVec;
+    if (slice_vec - ns_cap > kTailCapVec || ring) ns_cap = slice_vec - (ring ? 0 : kTailCapVec);
+    const long long stage_bytes = (ns_cap * 16 + 127) / 128 * 128;
+    long long stages = stage_bytes > 0 ? kMaxRingBytes / stage_bytes : 1;
     if (stages > kMaxStages) stages = kMaxStages;
     if (!ring && stages > 1) stages = 1;
     if (stages < 1) continue;
@@ -778,14 +854,12 @@ ClusterPlan plan_cluster(long long cols, bool ring) {
       cudaGetLastError();
       continue;
     }
-    // Score: resident CTAs (x2 for a ring of two or more buffers), and the smallest cluster whose slice is at most
-    // kSliceTarget bytes wins outright (fewer CTAs per row exchange less, three such slices fit an SM).
-    long long score = (long long)active * cl * (stages >= 2 ? 2 : 1);
-    if (stage_bytes <= kSliceTarget) score = (1LL << 40) + (kMaxCluster - cl);
-    if (active > 0 && score > best_score) {
+    const long long score = (long long)active * cl * (stages >= 2 ? 2 : 1);
+    if (active > 0 && score >= best_score) {
       best_score = score;
       best.cl = cl;
       best.slice = (int)slice;
+      best.ns_cap = (int)ns_cap;
       best.stages = (int)stages;
       best.stage_vec = (int)(stage_bytes / 16);
       best.active = active;
@@ -801,20 +875,20 @@ ClusterPlan plan_cluster(long long cols, bool ring) {
 
 template <typename T>
 int start_cluster(const ClusterPlan& p, const T* x, T* y, long long rows, long long cols, cudaStream_t s) {
-  auto kern = sm_cluster<T>;
+  auto kern = p.ring ? sm_cluster<T, true> : sm_cluster<T, false>;
   const int smem = p.stages * p.stage_vec * 16;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) {
     cudaGetLastError();
     return -2;
   }
   if (p.cl > 8) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  // One row per cluster (measured best: the whole row set in flight, three CTAs per SM), unless the rows exceed the
+  // One row per cluster (measured best: the whole row set in flight, four CTAs per SM), unless the rows exceed the
   // grid's y limit: then as many clusters as stay resident loop over the rows with a ring of slice buffers.
   const long long g = p.ring ? (rows < p.active ? rows : p.active) : rows;
   if (g > 65535) return -2;  // grid.y limit: the caller falls back
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = cluster_config(p.cl, (unsigned)g, smem, s, attr);
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, x, y, rows, cols, p.slice, p.stages, p.stage_vec);
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, x, y, rows, cols, p.slice, p.ns_cap, p.stages, p.stage_vec);
   if (err != cudaSuccess) return (int)err;
   return (int)cudaGetLastError();
 }

@@ -45,8 +45,8 @@ def test_config4_short_rows():
 
 # Column counts that reach every path: group (G = 4, 8, 16, 32), block, cluster (several cluster sizes), and the
 # stream fallback (cols not a multiple of the vector).
-COLS = [1, 4, 12, 16, 32, 100, 128, 256, 512, 1024, 2048, 8192, 16384, 20000, 32768, 65536, 100000, 262144,
-        1048576, 4194304,
+COLS = [1, 4, 12, 16, 32, 100, 128, 256, 512, 1024, 2048, 8192, 16384, 20000, 32768, 65536, 100000, 131072, 262144,
+        524288, 1048576, 4194304,
         13, 1001, 40001]
 
 
@@ -61,6 +61,20 @@ def test_shapes(dtype, cols):
     torch.cuda.synchronize()
     check()
     _check(x, y, f"{rows}x{cols} {dtype}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_rows_beyond_the_grid_limit(dtype):
+    """More rows than the cluster grid's y limit: resident clusters loop over the rows with a ring of slice buffers
+    (each slice partly staged, partly in registers). Rows spread over the batch are checked against the oracle."""
+    rows, cols = 65536 + 77, 16400 if dtype == torch.float32 else 32800
+    g = torch.Generator(device="cuda").manual_seed(11)
+    x = (torch.randn(rows, cols, generator=g, device="cuda") * 3).to(dtype)
+    y = softmax.softmax(x)
+    torch.cuda.synchronize()
+    pick = torch.tensor([0, 1, 2, 4095, 32768, 65534, 65535, 65536, rows - 2, rows - 1])
+    _check(x[pick].cpu(), y[pick], f"{rows}x{cols} {dtype} (ring)")
+    del x, y
 
 
 @pytest.mark.parametrize("cols", [128, 8192, 262144])
