@@ -56,7 +56,7 @@ typedef unsigned long long u64;
 #define CKB_TOPK_UNROLL_256 4
 #endif
 #ifndef CKB_TOPK_SLOTS_256
-#define CKB_TOPK_SLOTS_256 10
+#define CKB_TOPK_SLOTS_256 32
 #endif
 // The 256-thread shape for 2-byte elements: a shallower ring with more survivor slots (a 16-byte vector holds 8
 // elements, so more vectors pass the pre-filter per survivor and expansions are costlier).
@@ -71,6 +71,22 @@ typedef unsigned long long u64;
 #endif
 #ifndef CKB_TOPK_STRICT
 #define CKB_TOPK_STRICT 1
+#endif
+// 0: a survivor slot holds the recorded vector's index only, and the vector is read again (from L2, where the
+// streamed tile still is) when the slots are expanded, so a warp holds 32 slots in the shared memory that 10 slots
+// of vector + index took (1: vector and index; measured on B200, fp32 512 x 151936: 63.2 us with 10 such slots, 60.9
+// us with 32 index slots; 512 x 18992, a vocab shard at 8 GPUs: 27.1 -> 24.1 us).
+#ifndef CKB_TOPK_SLOT_DATA
+#define CKB_TOPK_SLOT_DATA 0
+#endif
+constexpr bool kSlotData = CKB_TOPK_SLOT_DATA != 0;
+// Segments of at least this many tiles ask for a compaction once a warp holds CKB_TOPK_SLOTS_FULL_LONG records (the
+// earlier raise of the bound pays over the long rest); shorter ones only when the slots are nearly full.
+#ifndef CKB_TOPK_LONG_TILES
+#define CKB_TOPK_LONG_TILES 16
+#endif
+#ifndef CKB_TOPK_SLOTS_FULL_LONG
+#define CKB_TOPK_SLOTS_FULL_LONG 12
 #endif
 #ifndef CKB_TOPK_OVF_BOUND
 #define CKB_TOPK_OVF_BOUND 1
@@ -119,7 +135,7 @@ struct Cfg {
   static constexpr int kSlots =  // vectors a warp records between compactions
       NT == 512 ? 12 : EB == 4 ? CKB_TOPK_SLOTS_256 : CKB_TOPK_SLOTS_256H;
   static constexpr int kSlotsFull = kSlots - 4;       // a warp holding this many asks for a compaction
-  static constexpr int kSlotBytes = kWarps * kSlots * 20;  // recorded vectors (16 bytes) and indices (4 bytes)
+  static constexpr int kSlotBytes = kWarps * kSlots * (kSlotData ? 20 : 4);  // recorded vectors (16 B), indices (4 B)
   static constexpr int kSmemBytes = kRingBytes + kCand * 8 + kPack * 8 + kSlotBytes;
   static constexpr int kMergeEntries = kRingBytes / 16;    // nseg * k: the merge ping-pongs between ring halves
   static constexpr int kMinBlocks = NT == 512 ? 2 : 4;
@@ -410,7 +426,7 @@ __device__ __forceinline__ int record(const TileRegs<T, NT, U>& t, float f_lo, u
     if (maybe) {
       const int pos = wcnt + __popc(bal & below);
       if (pos < Cfg<NT, sizeof(T)>::kSlots) {
-        wslot[pos] = t.r[u];
+        if (kSlotData) wslot[pos] = t.r[u];
         widx[pos] = (unsigned)v;
       }
     }
@@ -431,7 +447,7 @@ __device__ __forceinline__ void expand(const uint4* wslot, const unsigned* widx,
   uint4 r = make_uint4(0u, 0u, 0u, 0u);
   unsigned idx0 = 0u, take = 0u;
   if (lane < n) {
-    r = wslot[lane];
+    r = kSlotData ? wslot[lane] : __ldcg(wslot + widx[lane]);
     idx0 = base_idx + widx[lane] * (unsigned)V;
 #pragma unroll
     for (int e = 0; e < V; ++e)
@@ -457,7 +473,7 @@ __device__ __forceinline__ void for_each_recorded(const uint4* wslot, const unsi
   const T* tag = nullptr;
   const int lane = threadIdx.x & 31;
   if (lane >= n) return;
-  const uint4 r = wslot[lane];
+  const uint4 r = kSlotData ? wslot[lane] : __ldcg(wslot + widx[lane]);
   const unsigned idx0 = base_idx + widx[lane] * (unsigned)V;
 #pragma unroll
   for (int e = 0; e < V; ++e) {
@@ -846,7 +862,8 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   u64* tmp = cand + kCand;  // compaction scratch: kPack composites or the radix histogram
   unsigned char* slots = smem_raw + kRingBytes + (kCand + kPack) * 8;
   uint4* wslot = reinterpret_cast<uint4*>(slots) + (threadIdx.x >> 5) * kSlots;  // this warp's recorded vectors
-  unsigned* widx = reinterpret_cast<unsigned*>(slots + kWarps * kSlots * 16) + (threadIdx.x >> 5) * kSlots;
+  unsigned* widx = reinterpret_cast<unsigned*>(slots + (kSlotData ? kWarps * kSlots * 16 : 0)) +
+                   (threadIdx.x >> 5) * kSlots;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long long row = blockIdx.y;
@@ -862,6 +879,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
   const int v0 = min(nvr, seg * segv);
   const int nv = min(nvr, v0 + segv) - v0;
   const uint4* body = reinterpret_cast<const uint4*>(rowp + head) + v0;
+  const uint4* const rec_src = kSlotData ? wslot : body;  // where an expansion reads a recorded vector
 
   TileRegs<T, NT, kU> t;
   t.nv = nv;
@@ -879,6 +897,8 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
 
   const int ntiles = max(1, (nv + kTileVecs - 1) / kTileVecs);
   const int full_tiles = nv / kTileVecs;  // tiles whose every vector lies in the segment
+  const int slots_full = ntiles >= CKB_TOPK_LONG_TILES && CKB_TOPK_SLOTS_FULL_LONG < kSlotsFull
+                             ? CKB_TOPK_SLOTS_FULL_LONG : kSlotsFull;
   // Tile j's vectors of this thread into ring stage `stage`; one commit group per tile (empty past the last tile).
   auto issue = [&](int j, int stage) {
     if (j < ntiles) {
@@ -992,14 +1012,14 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
     if (ntop + filled + kWarps * kSlots * V <= kCand) {  // every composite of every slot fits: no count needed
       if (tid == 0) s_cnt = 0;
       __syncthreads();
-      expand<T, kCand>(wslot, widx, n, t.base_idx, lo, cand, ntop + filled, &s_cnt);
+      expand<T, kCand>(rec_src, widx, n, t.base_idx, lo, cand, ntop + filled, &s_cnt);
       __syncthreads();
       take_count();
       return;
     }
     if (tid == 0) s_cnt = 0;
     __syncthreads();
-    expand<T, kCand>(wslot, widx, n, t.base_idx, lo, nullptr, 0, &s_cnt);
+    expand<T, kCand>(rec_src, widx, n, t.base_idx, lo, nullptr, 0, &s_cnt);
     __syncthreads();
     const int need = s_cnt;
     __syncthreads();
@@ -1007,13 +1027,13 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
     if (ntop + filled + need > kCand) compact_all(-1.0f);
     if (ntop + filled + need > kCand) {
       const u64 edge = radix_edge<NT>(
-          [&](auto&& f) { for_each_recorded<T>(wslot, widx, n, t.base_idx, lo, f); }, (unsigned)k, kCand - ntop,
+          [&](auto&& f) { for_each_recorded<T>(rec_src, widx, n, t.base_idx, lo, f); }, (unsigned)k, kCand - ntop,
           reinterpret_cast<unsigned*>(tmp), warp_tot, &s_bin, &s_above);
       set_lo(edge, false);
     }
     if (tid == 0) s_cnt = 0;
     __syncthreads();
-    expand<T, kCand>(wslot, widx, n, t.base_idx, lo, cand, ntop + filled, &s_cnt);
+    expand<T, kCand>(rec_src, widx, n, t.base_idx, lo, cand, ntop + filled, &s_cnt);
     __syncthreads();
     take_count();
   };
@@ -1090,7 +1110,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
       load(j, rs);
       const int before = wcnt;
       wcnt = j < full_tiles ? record<true>(t, f_lo, wslot, widx, wcnt) : record<false>(t, f_lo, wslot, widx, wcnt);
-      if (lane == 0 && wcnt >= kSlotsFull) atomicOr(&s_flag[fs], wcnt > kSlots ? 3 : 1);
+      if (lane == 0 && wcnt >= slots_full) atomicOr(&s_flag[fs], wcnt > kSlots ? 3 : 1);
       const int fnext = fs == 2 ? 0 : fs + 1;
       if (tid == 0) s_flag[fnext] = 0;  // its last reads came before the barrier of tile j - 1
       __syncthreads();
