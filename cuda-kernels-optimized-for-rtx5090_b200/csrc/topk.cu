@@ -49,14 +49,24 @@ typedef unsigned long long u64;
 #ifndef CKB_TOPK_UNROLL
 #define CKB_TOPK_UNROLL 4
 #endif
+// fp32 rows: 20 KB tiles in a 2-stage ring (one tile in flight while one is filtered). Measured on B200 at 512 x
+// 151936: 16 KB x 3 stages 60.8 us, 20 KB x 2 58.6, 24 KB x 2 58.5 (spills), 12 KB x 4 61.8; fewer barriers per
+// byte outweigh the shallower ring at four CTAs per SM.
 #ifndef CKB_TOPK_STAGES_256
-#define CKB_TOPK_STAGES_256 3
+#define CKB_TOPK_STAGES_256 2
 #endif
 #ifndef CKB_TOPK_UNROLL_256
-#define CKB_TOPK_UNROLL_256 4
+#define CKB_TOPK_UNROLL_256 5
 #endif
 #ifndef CKB_TOPK_SLOTS_256
 #define CKB_TOPK_SLOTS_256 32
+#endif
+// Candidate buffer of the 256-thread shape (the running top k and the survivors behind it). 1280 lets every warp's
+// 32 slots expand in one pass (k + 8 warps x 32 vectors x 4 composites fits with room to spare) and a tile of heavy
+// ties collect without the overflow path. Measured on B200, fp32 512 x 151936: 512 entries 58.9 us, 1024 58.9, 1280
+// 56.7, 1536 56.6; few-valued rows 137.2 -> 113.1 us, ascending rows 551 -> 380 us.
+#ifndef CKB_TOPK_CAND_256
+#define CKB_TOPK_CAND_256 1280
 #endif
 // The 256-thread shape for 2-byte elements: a shallower ring with more survivor slots (a 16-byte vector holds 8
 // elements, so more vectors pass the pre-filter per survivor and expansions are costlier).
@@ -80,10 +90,10 @@ typedef unsigned long long u64;
 #define CKB_TOPK_SLOT_DATA 0
 #endif
 constexpr bool kSlotData = CKB_TOPK_SLOT_DATA != 0;
-// Segments of at least this many tiles ask for a compaction once a warp holds CKB_TOPK_SLOTS_FULL_LONG records (the
-// earlier raise of the bound pays over the long rest); shorter ones only when the slots are nearly full.
-#ifndef CKB_TOPK_LONG_TILES
-#define CKB_TOPK_LONG_TILES 16
+// Segments of at least this many elements ask for a compaction once a warp holds CKB_TOPK_SLOTS_FULL_LONG records
+// (the earlier raise of the bound pays over the long rest); shorter ones only when the slots are nearly full.
+#ifndef CKB_TOPK_LONG_ELEMS
+#define CKB_TOPK_LONG_ELEMS 65536
 #endif
 #ifndef CKB_TOPK_SLOTS_FULL_LONG
 #define CKB_TOPK_SLOTS_FULL_LONG 12
@@ -127,7 +137,8 @@ struct Cfg {
       NT == 512 ? CKB_TOPK_UNROLL : EB == 4 ? CKB_TOPK_UNROLL_256 : CKB_TOPK_UNROLL_256H;
   static constexpr int kTileVecs = NT * kU;       // thread t holds vectors u * NT + t of a tile
   static constexpr int kRingBytes = kStages * kTileVecs * 16;
-  static constexpr int kCand = 2 * kMaxK;         // running top k + survivors since the last compaction
+  static constexpr int kCand = NT == 512 ? 2 * kMaxK : CKB_TOPK_CAND_256;  // running top k + survivors since the
+                                                                              // last compaction
   static constexpr int kPack = kMaxK;             // compaction scratch entries
   static constexpr int kDigit = NT == 512 ? 10 : 9;
   static constexpr int kRadixBins = 1 << kDigit;
@@ -417,20 +428,30 @@ __device__ __forceinline__ int record(const TileRegs<T, NT, U>& t, float f_lo, u
                                       int wcnt) {
   const T* tag = nullptr;
   const unsigned below = (1u << (threadIdx.x & 31)) - 1u;
+  // The U tests and ballots are independent; one branch skips the (common) tile slice with nothing to record.
+  bool maybe[U];
+  unsigned bal[U], any = 0u;
 #pragma unroll
   for (int u = 0; u < U; ++u) {
     const int v = t.vb + u * NT;
-    const bool maybe = (kFull || v < t.nv) && !(vec_max_nan(t.r[u], tag) < f_lo);
-    const unsigned bal = __ballot_sync(0xffffffffu, maybe);
-    if (bal == 0u) continue;
-    if (maybe) {
-      const int pos = wcnt + __popc(bal & below);
+    maybe[u] = (kFull || v < t.nv) && !(vec_max_nan(t.r[u], tag) < f_lo);
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    bal[u] = __ballot_sync(0xffffffffu, maybe[u]);
+    any |= bal[u];
+  }
+  if (any == 0u) return wcnt;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    if (maybe[u]) {
+      const int pos = wcnt + __popc(bal[u] & below);
       if (pos < Cfg<NT, sizeof(T)>::kSlots) {
         if (kSlotData) wslot[pos] = t.r[u];
-        widx[pos] = (unsigned)v;
+        widx[pos] = (unsigned)(t.vb + u * NT);
       }
     }
-    wcnt += __popc(bal);
+    wcnt += __popc(bal[u]);
   }
   return wcnt;
 }
@@ -897,7 +918,7 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
 
   const int ntiles = max(1, (nv + kTileVecs - 1) / kTileVecs);
   const int full_tiles = nv / kTileVecs;  // tiles whose every vector lies in the segment
-  const int slots_full = ntiles >= CKB_TOPK_LONG_TILES && CKB_TOPK_SLOTS_FULL_LONG < kSlotsFull
+  const int slots_full = (long long)nv * V >= CKB_TOPK_LONG_ELEMS && CKB_TOPK_SLOTS_FULL_LONG < kSlotsFull
                              ? CKB_TOPK_SLOTS_FULL_LONG : kSlotsFull;
   // Tile j's vectors of this thread into ring stage `stage`; one commit group per tile (empty past the last tile).
   auto issue = [&](int j, int stage) {
