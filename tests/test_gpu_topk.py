@@ -137,7 +137,7 @@ def test_wide_batch_segments(dtype, nseg):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("k", [50, 64, 65])
+@pytest.mark.parametrize("k", [50, 64, 65, 200, 256])
 def test_many_rows_edge_cases(dtype, k):
     """300 rows (at least two per SM: the 256-thread shape, and for k <= 64 its warp-local variant) mixing random
     rows, few-valued rows (ties everywhere), rising and falling rows (a tile overflowing a warp's slots; a speculative
@@ -157,6 +157,22 @@ def test_many_rows_edge_cases(dtype, k):
     x = x.to(dtype)
     vv, ii = topk.topk(x.cuda(), k)
     _check(x, k, vv, ii, f"many rows k={k}")
+
+
+@pytest.mark.parametrize("k", [1, 50, 256])
+def test_long_rows_one_wave_with_ties_and_rising_rows(k):
+    """The config's shape class (at least two rows per SM, rows long enough to count as long segments): random,
+    few-valued, rising and falling rows side by side, fp32, every row bit-exact for k up to the 256-thread bound."""
+    g = torch.Generator().manual_seed(1000 + k)
+    rows, cols = 304, 98305
+    x = torch.randn(rows, cols, generator=g) * 3
+    up = torch.arange(cols, dtype=torch.float32)
+    for r in range(0, rows, 8):
+        x[r + 1] = torch.randint(0, 8, (cols,), generator=g).float()
+        x[r + 2] = up
+        x[r + 3] = up.flip(0)
+    vv, ii = topk.topk(x.cuda(), k)
+    _check(x, k, vv, ii, f"long rows k={k}")
 
 
 def test_repeated_calls_reuse_workspace_and_counters():
