@@ -68,13 +68,13 @@ typedef unsigned long long u64;
 #ifndef CKB_TOPK_CAND_256
 #define CKB_TOPK_CAND_256 1280
 #endif
-// The 256-thread shape for 2-byte elements: a shallower ring with more survivor slots (a 16-byte vector holds 8
-// elements, so more vectors pass the pre-filter per survivor and expansions are costlier).
+// The 256-thread shape for 2-byte elements: 20 KB tiles (10240 elements) in a 2-stage ring as for fp32 (measured at
+// 512 x 151936 bf16: 16 KB tiles 44.9 us, 20 KB 43.9 us, 12 KB x 3 stages 45.7 us).
 #ifndef CKB_TOPK_STAGES_256H
 #define CKB_TOPK_STAGES_256H 2
 #endif
 #ifndef CKB_TOPK_UNROLL_256H
-#define CKB_TOPK_UNROLL_256H 4
+#define CKB_TOPK_UNROLL_256H 5
 #endif
 #ifndef CKB_TOPK_SLOTS_256H
 #define CKB_TOPK_SLOTS_256H 32
@@ -97,6 +97,9 @@ constexpr bool kSlotData = CKB_TOPK_SLOT_DATA != 0;
 #endif
 #ifndef CKB_TOPK_SLOTS_FULL_LONG
 #define CKB_TOPK_SLOTS_FULL_LONG 12
+#endif
+#ifndef CKB_TOPK_SLOTS_FULL_LONG_H
+#define CKB_TOPK_SLOTS_FULL_LONG_H 20  // 2-byte elements: a vector holds 8, so more vectors pass per survivor
 #endif
 #ifndef CKB_TOPK_OVF_BOUND
 #define CKB_TOPK_OVF_BOUND 1
@@ -161,12 +164,14 @@ struct Cfg {
   static_assert(kSlots <= 32, "a warp expands its slots one per lane");
   static_assert(kCtasPerSm >= 1, "one CTA's shared memory fits an SM");
 };
-// Segments per row that every k fits in every shape's merge.
+// Segments per row that every k fits in every shape's merge, and at most 8 (measured on B200 at 1 x 128256: 8
+// segments 14.0 us fp32 / 11.2 us bf16, 10 segments 14.3 / 11.6 us: the last CTA's merge grows with the lists).
 template <int NT, int EB>
 constexpr int seg_cap() { return Cfg<NT, EB>::kMergeEntries / Cfg<NT, EB>::kMaxK; }
 constexpr int min2(int a, int b) { return a < b ? a : b; }
 #ifndef CKB_TOPK_MAX_SEG
-#define CKB_TOPK_MAX_SEG min2(min2(seg_cap<256, 4>(), seg_cap<256, 2>()), min2(seg_cap<512, 4>(), seg_cap<512, 2>()))
+#define CKB_TOPK_MAX_SEG \
+  min2(8, min2(min2(seg_cap<256, 4>(), seg_cap<256, 2>()), min2(seg_cap<512, 4>(), seg_cap<512, 2>())))
 #endif
 constexpr int kMaxSeg = CKB_TOPK_MAX_SEG;
 
@@ -918,8 +923,9 @@ __global__ void __launch_bounds__(NT, Cfg<NT>::kMinBlocks) topk_stream(const Seg
 
   const int ntiles = max(1, (nv + kTileVecs - 1) / kTileVecs);
   const int full_tiles = nv / kTileVecs;  // tiles whose every vector lies in the segment
-  const int slots_full = (long long)nv * V >= CKB_TOPK_LONG_ELEMS && CKB_TOPK_SLOTS_FULL_LONG < kSlotsFull
-                             ? CKB_TOPK_SLOTS_FULL_LONG : kSlotsFull;
+  constexpr int kFullLong = sizeof(T) == 2 ? CKB_TOPK_SLOTS_FULL_LONG_H : CKB_TOPK_SLOTS_FULL_LONG;
+  const int slots_full =
+      (long long)nv * V >= CKB_TOPK_LONG_ELEMS && kFullLong < kSlotsFull ? kFullLong : kSlotsFull;
   // Tile j's vectors of this thread into ring stage `stage`; one commit group per tile (empty past the last tile).
   auto issue = [&](int j, int stage) {
     if (j < ntiles) {
