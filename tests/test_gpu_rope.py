@@ -2,7 +2,8 @@
 
 Cache mode uses the same cos/sin bits and the same roundings as the oracle, so it must match bit for bit on every
 input (the integer-valued config is the north star's exact-match case). Sincos mode computes cos/sin on the device
-with sincosf: tolerance 1 ulp of the output dtype plus 1e-6 * (|x_i| + |x_{i+h}|) for the cos/sin difference.
+with sincosf: 1 ulp of the output dtype wherever the rotation does not cancel, else 1e-6 * (|x_i| + |x_{i+h}|) for
+the cos/sin difference.
 """
 
 import ctypes
@@ -80,8 +81,12 @@ def _sincos_check(got, x, want):
     mag = np.abs(xf[..., :h]) + np.abs(xf[..., h:])
     mag = np.concatenate([mag, mag], axis=-1)
     d = ulp_distance(g, w, got.dtype)
-    # 1 ulp of the dtype, or an absolute error explained by cos/sin differing by a few fp32 ulps
-    ok = (d <= 1) | (np.abs(g - w) <= 1e-6 * mag + 2 ** -24)
+    # Within 1 ulp of the dtype wherever the rotation does not cancel (|out| >= (|x_i| + |x_{i+h}|) / 64). Under
+    # deep cancellation a cos/sin that differs from the cached value by an fp32 ulp moves the tiny result by many of
+    # its own ulps; there the bound is absolute: 1e-6 * (|x_i| + |x_{i+h}|) (measured on the full config: 160 of
+    # 167.8 M outputs beyond 1 ulp, all with |out| <= 2e-5 * (|x_i| + |x_{i+h}|)).
+    cancels = np.abs(w) < mag / 64
+    ok = (d <= 1) | (cancels & (np.abs(g - w) <= 1e-6 * mag + 2 ** -24))
     assert ok.all(), f"{(~ok).sum()} elements beyond tolerance"
     return (d == 0).mean()
 
