@@ -107,3 +107,20 @@ def test_noalloc_split_plans_stay_small():
                 assert nseg == 1 or rows * nseg * 512 <= 491520, (rows, cols, nseg)
     for rows in (296, 512, 1000, 65535):
         assert tk.plan(rows, 151936, 0, 256, 4, 2048) == 151936
+
+
+def test_recorded_wrapper_calls_match_the_declared_signatures():
+    """The fixture of the reference wrappers' calls (tests/golden/dropin_calls.json, replayed on the GPU by
+    test_gpu_dropin_replay.py) binds exactly the argument and result types this library declares for each symbol."""
+    import json
+
+    from ckb200 import _native
+
+    fixture = json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "dropin_calls.json")))
+    for op, rec in fixture.items():
+        assert rec["calls"], op
+        for call in rec["calls"]:
+            res, args = _native.SIGNATURES[op][call["fn"]]
+            assert [t.__name__ for t in args] == call["argtypes"], (op, call["fn"])
+            assert res.__name__ == call["restype"], (op, call["fn"])
+            assert len(call["args"]) == len(args), (op, call["fn"])
