@@ -25,7 +25,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path[:0] = [ROOT, os.path.join(ROOT, "tests"), os.path.join(ROOT, "cuda-kernels-optimized-for-rtx5090_b200")]
 
-from dropin_inputs import OUTPUTS, make_inputs  # noqa: E402
+from dropin_inputs import CASES, OUTPUTS, make_inputs  # noqa: E402
 
 
 class _Stream:
@@ -55,13 +55,13 @@ def _tensors(obj, prefix, out):
         out.setdefault(obj.data_ptr(), (prefix, obj))
     elif isinstance(obj, dict):
         for k, v in obj.items():
-            _tensors(v, f"{prefix}{k}" if not prefix.endswith(":") else f"{prefix}{k}", out)
+            _tensors(v, f"{prefix}{k}", out)
     elif isinstance(obj, (list, tuple)):
         for i, v in enumerate(obj):
             _tensors(v, f"{prefix}{i}", out)
 
 
-def record(op, ref, lib_dir):
+def record(op, case, ref, lib_dir):
     os.environ["CKOPT_BUILD_DIR"] = lib_dir
     spec = importlib.util.spec_from_file_location(f"reference_{op}_candidate", os.path.join(ref, op, "candidate.py"))
     mod = importlib.util.module_from_spec(spec)
@@ -71,7 +71,7 @@ def record(op, ref, lib_dir):
     real_stream = torch.cuda.current_stream
     torch.cuda.current_stream = lambda *a, **k: _Stream()
     try:
-        inputs = make_inputs(op)
+        inputs = make_inputs(op, case)
         outputs = mod.run(inputs)
     finally:
         torch.cuda.current_stream = real_stream
@@ -120,7 +120,7 @@ def main():
     fixture = {}
     for op in ("rmsnorm", "rope", "topk"):
         build.build(ops=(op,))
-        fixture[op] = record(op, a.ref, os.path.dirname(build.lib_path(op)))
+        fixture[op] = {case: record(op, case, a.ref, os.path.dirname(build.lib_path(op))) for case in CASES[op]}
     with open(a.out, "w") as f:
         json.dump(fixture, f, indent=1)
         f.write("\n")

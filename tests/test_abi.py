@@ -117,10 +117,11 @@ def test_recorded_wrapper_calls_match_the_declared_signatures():
     from ckb200 import _native
 
     fixture = json.load(open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "dropin_calls.json")))
-    for op, rec in fixture.items():
-        assert rec["calls"], op
-        for call in rec["calls"]:
-            res, args = _native.SIGNATURES[op][call["fn"]]
-            assert [t.__name__ for t in args] == call["argtypes"], (op, call["fn"])
-            assert res.__name__ == call["restype"], (op, call["fn"])
-            assert len(call["args"]) == len(args), (op, call["fn"])
+    for op, cases in fixture.items():
+        for case, rec in cases.items():
+            assert rec["calls"], (op, case)
+            for call in rec["calls"]:
+                res, args = _native.SIGNATURES[op][call["fn"]]
+                assert [t.__name__ for t in args] == call["argtypes"], (op, case, call["fn"])
+                assert res.__name__ == call["restype"], (op, case, call["fn"])
+                assert len(call["args"]) == len(args), (op, case, call["fn"])

@@ -15,7 +15,7 @@ import pytest
 import torch
 
 from ckb200 import build, rmsnorm, rope, topk
-from dropin_inputs import OUTPUTS, make_inputs
+from dropin_inputs import CASES, OUTPUTS, make_inputs
 from helpers import assert_ulp, bits_equal
 from oracle import rmsnorm as ormsnorm
 from oracle import rope as orope
@@ -27,9 +27,9 @@ DTYPES = {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch
           "int64": torch.int64}
 
 
-def _replay(op):
-    rec = json.load(open(FIXTURE))[op]
-    inputs = {k: v.cuda() for k, v in make_inputs(op).items()}
+def _replay(op, case):
+    rec = json.load(open(FIXTURE))[op][case]
+    inputs = {k: v.cuda() for k, v in make_inputs(op, case).items()}
     outputs = {k: torch.empty(s["shape"], dtype=DTYPES[s["dtype"]], device="cuda") for k, s in rec["outputs"].items()}
     allocs = {k: (torch.zeros if s["zero"] else torch.empty)(s["shape"], dtype=DTYPES[s["dtype"]], device="cuda")
               for k, s in rec["allocs"].items()}
@@ -53,26 +53,29 @@ def _replay(op):
             assert rc == 0, f"{op}: launch returned {rc}"
     torch.cuda.synchronize()
     assert sorted(outputs) == sorted(OUTPUTS[op])
-    return make_inputs(op), inputs, outputs
+    return make_inputs(op, case), inputs, outputs
 
 
-def test_rmsnorm_wrapper_calls():
-    host, dev, out = _replay("rmsnorm")
+@pytest.mark.parametrize("case", CASES["rmsnorm"])
+def test_rmsnorm_wrapper_calls(case):
+    host, dev, out = _replay("rmsnorm", case)
     ours = rmsnorm.run(dev)["y"]
     assert bits_equal(out["y"], ours)
-    assert_ulp(out["y"], ormsnorm.rmsnorm(host["x"]), torch.bfloat16, 1, "replayed rmsnorm")
+    assert_ulp(out["y"], ormsnorm.rmsnorm(host["x"]), host["x"].dtype, 1, f"replayed rmsnorm {case}")
 
 
-def test_rope_wrapper_calls():
-    host, dev, out = _replay("rope")
+@pytest.mark.parametrize("case", CASES["rope"])
+def test_rope_wrapper_calls(case):
+    host, dev, out = _replay("rope", case)
     ours = rope.run(dev)
     wq, wk = orope.rope(host["q"], host["k"], host["cos"], host["sin"], host["position_ids"])
     assert bits_equal(out["q_out"], ours["q_out"]) and bits_equal(out["k_out"], ours["k_out"])
     assert bits_equal(out["q_out"], wq) and bits_equal(out["k_out"], wk)
 
 
-def test_topk_wrapper_calls():
-    host, dev, out = _replay("topk")
+@pytest.mark.parametrize("case", CASES["topk"])
+def test_topk_wrapper_calls(case):
+    host, dev, out = _replay("topk", case)
     ours = topk.run(dev)
     assert torch.equal(out["indices"], ours["indices"]) and bits_equal(out["values"], ours["values"])
     wv, wi = otopk.topk(host["x"], 50)
